@@ -1,0 +1,505 @@
+"""Benchmark of the gpu-power-lab load generators on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload memstream|sgemm|fp8|nvfp4|powervirus]
+
+Default workload: the memstream STREAM triad a = b + 3.0 * c over three FP32
+arrays of 2^30 elements (4 GiB each; b, c ~ U[0,1) seeded). One step = one
+triad launch over the whole arrays. Every GPU runs its own replica (the
+workload does not shard): value = bytes moved by all ranks / max-over-ranks
+device time. Inputs are 12 GiB per step, far above the 126 MB L2, so no L2
+flush is needed between steps.
+
+Other rungs (--workload): sgemm (FP32 1024^3), fp8 (E4M3 8192^3), nvfp4
+(E2M1 16384^3) report TFLOP/s; powervirus reports sustained watts.
+
+--impl reference times the reference path's CPU implementation on the host
+cores (the oracle port of the triad, all threads), rank 0 only.
+
+Prints ONE JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+PKG = REPO / "gpu-power-lab_b200"
+sys.path.insert(0, str(PKG))
+
+TRIAD_N = 1 << 30
+TRIAD_S = 3.0
+TRIAD_BYTES = 12 * TRIAD_N  # read b, read c, write a (runner/src/workload_util.c:43-47)
+
+# dram__bytes_read.sum + dram__bytes_write.sum per launch from ncu captures
+# (profiles/*.md, scaled to the full launch where the capture was smaller).
+NCU_TRAFFIC = {
+    "memstream": None,
+    "sgemm": None,
+    "fp8": None,
+    "nvfp4": None,
+}
+
+NOMINAL_TFLOPS = {"fp8": 4500.0, "nvfp4": 9000.0, "sgemm": 148 * 128 * 2 * 1.965e9 / 1e12}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["memstream", "sgemm", "fp8", "nvfp4", "powervirus"],
+                    default="memstream")
+    ap.add_argument("--kernel", choices=["vec4", "bulk"], default="vec4",
+                    help="memstream kernel variant")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------ distributed plumbing
+
+class Dist:
+    def __init__(self, n_gpus: int):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+
+            import torch
+            import torch.distributed as dist
+
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg:
+            import torch
+
+            t = torch.zeros(1, device="cuda")
+            self.pg.all_reduce(t)
+            torch.cuda.synchronize()
+
+    def max(self, x: float) -> float:
+        if not self.pg:
+            return x
+        import torch
+
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+# ------------------------------------------------------------ clocks during the timed region
+
+REASONS = {
+    0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+    0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+    0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+}
+
+
+class ClockSampler:
+    """NVML sampling thread: SM clock, throttle reasons and power, every 25 ms."""
+
+    def __init__(self, device_index: int):
+        self.idx = device_index
+        self.samples = []
+        self._stop = threading.Event()
+        self._thr = None
+        self.ok = False
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_sm = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.limit_w = pynvml.nvmlDeviceGetEnforcedPowerLimit(self.h) / 1000.0
+            self.ok = True
+        except Exception:
+            self.max_sm = None
+            self.limit_w = None
+
+    def _sample(self):
+        nv = self.nv
+        sm = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+        try:
+            reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+        except Exception:
+            reasons = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+        power = nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0
+        self.samples.append((time.time(), sm, reasons, power))
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self._sample()
+            except Exception:
+                pass
+            self._stop.wait(0.025)
+
+    def start(self):
+        if self.ok:
+            self._thr = threading.Thread(target=self._run, daemon=True)
+            self._thr.start()
+
+    def stop(self):
+        if self._thr:
+            self._stop.set()
+            self._thr.join()
+            if not self.samples:
+                try:
+                    self._sample()
+                except Exception:
+                    pass
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_sm, "reasons": [], "samples": 0}
+        sms = sorted(s[1] for s in self.samples)
+        mask = 0
+        for s in self.samples:
+            mask |= int(s[2])
+        reasons = [name for bit, name in REASONS.items() if mask & bit and bit != 0x1]
+        pw = sorted(s[3] for s in self.samples)
+        return {
+            "sm_mhz": sms[len(sms) // 2],
+            "sm_max_mhz": self.max_sm,
+            "reasons": reasons,
+            "samples": len(self.samples),
+            "power_w_median": round(pw[len(pw) // 2], 1),
+            "power_limit_w": self.limit_w,
+        }
+
+
+def measured_peaks() -> dict:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        d["_source"] = "measured"
+        return d
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "_source": "fallback"}
+
+
+# ------------------------------------------------------------ CPU baseline (oracle port)
+
+def cpu_triad_gbps(seconds: float, n: int = 1 << 28, threads: int = 0) -> dict:
+    """The host triad a = fmaf(s, c, b) (the oracle's restatement of the
+    triad) over n elements, repeated for about `seconds`, all cores."""
+    sys.path.insert(0, str(REPO / "oracle"))
+    import numpy as np
+    import oracle
+
+    b = oracle.uniform_f32(n, seed=101)
+    c = oracle.uniform_f32(n, seed=202)
+    a = np.empty_like(b)
+    nthreads = threads or oracle.max_threads()
+    oracle.triad_into(a, b, c, TRIAD_S, nthreads)  # first touch
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        oracle.triad_into(a, b, c, TRIAD_S, nthreads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return {"value": round(12 * n * reps / el / 1e9, 2), "unit": "GB/s", "cores": nthreads, "kind": "port",
+            "sample": f"{reps} host triads over 3 x 2^{n.bit_length() - 1} FP32 ({el:.1f} s)"}
+
+
+# ------------------------------------------------------------ memstream
+
+def bench_memstream(args, dist: Dist) -> dict:
+    import torch
+    import gplk
+
+    dev = torch.device("cuda", dist.local)
+    torch.cuda.set_device(dev)
+    gplk.lib()
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + dist.rank)
+    b = torch.rand(TRIAD_N, device=dev, generator=g)
+    c = torch.rand(TRIAD_N, device=dev, generator=g)
+    a = torch.empty(TRIAD_N, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    bulk = args.kernel == "bulk"
+
+    def step():
+        gplk.triad(a, b, c, TRIAD_S, stream=stream, bulk=bulk)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(dist.local)
+    dist.barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    sampler.stop()
+    ms = e0.elapsed_time(e1)
+    ms_max = dist.max(ms)
+    code, site = gplk.status_read()
+    if code != 0:
+        raise RuntimeError(f"device status {code} at {site:#x}")
+
+    per_launch_s = ms / 1e3 / args.steps
+    achieved = TRIAD_BYTES / per_launch_s / 1e9
+    peaks = measured_peaks()
+    value = dist.world * TRIAD_BYTES * args.steps / (ms_max / 1e3) / 1e9
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = memstream_e2e(a, b, c, stream, bulk, dist, steps=3)
+
+    traffic = NCU_TRAFFIC["memstream"]
+    out = {
+        "metric": "memstream triad GB/s",
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": dist.world,
+        "steps": args.steps,
+        "warmup": max(args.warmup, 3),
+        "ms_per_step": round(ms_max / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic: b, c ~ U[0,1) from torch's seeded generator, s = 3.0",
+        "config": {"workload": "memstream STREAM triad a = b + 3.0*c, FP32, 3 x 2^30 elements (4 GiB each)",
+                   "elements": TRIAD_N, "bytes_per_step_per_gpu": TRIAD_BYTES,
+                   "kernel": "triad_bulk" if bulk else "triad_vec4",
+                   "l2": "inputs (12 GiB per step) larger than the 126 MB L2; no flush",
+                   "parallelism": f"replicas x{dist.world} (the workload does not shard)"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
+                     "peak_source": f"{peaks['_source']} hbm_gbs (burst copy)",
+                     "algorithmic_bytes_per_launch": TRIAD_BYTES},
+        "clocks": sampler.summary(),
+        "gpu_launches": args.steps,
+    }
+    if e2e:
+        out["e2e"] = e2e
+    return out
+
+
+def memstream_e2e(a, b, c, stream, bulk, dist: Dist, steps: int) -> dict:
+    """The same triad through the C ABI with host buffers: every step copies
+    b and c from pinned host memory, runs the triad and reads a back."""
+    import torch
+    import gplk
+
+    hb = torch.empty(TRIAD_N, dtype=torch.float32, pin_memory=True)
+    hc = torch.empty(TRIAD_N, dtype=torch.float32, pin_memory=True)
+    ha = torch.empty(TRIAD_N, dtype=torch.float32, pin_memory=True)
+    hb.copy_(b, non_blocking=False)
+    hc.copy_(c, non_blocking=False)
+
+    def step():
+        b.copy_(hb, non_blocking=True)
+        c.copy_(hc, non_blocking=True)
+        gplk.triad(a, b, c, TRIAD_S, stream=stream, bulk=bulk)
+        ha.copy_(a, non_blocking=True)
+
+    step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = dist.max(e0.elapsed_time(e1))
+    value = dist.world * TRIAD_BYTES * steps / (ms / 1e3) / 1e9
+    return {"value": round(value, 2), "unit": "GB/s", "h2d_bytes_per_step": 8 * TRIAD_N,
+            "d2h_bytes_per_step": 4 * TRIAD_N, "steps": steps,
+            "note": "pinned host b, c -> device, triad, device a -> pinned host, per step"}
+
+
+# ------------------------------------------------------------ GEMM rungs
+
+def bench_gemm(args, dist: Dist) -> dict:
+    import torch
+    import gplk
+
+    dev = torch.device("cuda", dist.local)
+    torch.cuda.set_device(dev)
+    gplk.lib()
+    g = torch.Generator(device=dev)
+    g.manual_seed(7 + dist.rank)
+    stream = torch.cuda.current_stream(dev)
+    w = args.workload
+    if w == "sgemm":
+        n = 1024
+        A = torch.rand(n, n, device=dev, generator=g) * 2 - 1
+        B = torch.rand(n, n, device=dev, generator=g) * 2 - 1
+        C = torch.empty(n, n, device=dev)
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+        def step():
+            flush.zero_()  # 256 MiB write: evicts the 12 MiB working set from L2
+            gplk.sgemm(A, B, C, stream=stream)
+
+        dtype, workload = "f32", "FP32 SGEMM C = A*B row-major, M=N=K=1024, U[-1,1)"
+        launches_per_step = 2
+    else:
+        n = 8192 if w == "fp8" else 16384
+        if w == "fp8":
+            A = (torch.randn(n, n, device=dev, generator=g) * 32).clamp(-448, 448).to(torch.float8_e4m3fn).view(torch.uint8)
+            B = (torch.randn(n, n, device=dev, generator=g) * 32).clamp(-448, 448).to(torch.float8_e4m3fn).view(torch.uint8)
+            D = torch.empty(n, n, dtype=torch.bfloat16, device=dev)
+            s = torch.ones(1, device=dev)
+
+            def step():
+                gplk.gemm_fp8_tn(A, B, D, s, s, stream=stream)
+
+            dtype, workload = "e4m3", "FP8 E4M3 TN GEMM M=N=K=8192, per-tensor scales, BF16 out"
+        else:
+            A = torch.randint(0, 256, (n, n // 2), dtype=torch.uint8, device=dev, generator=g)
+            B = torch.randint(0, 256, (n, n // 2), dtype=torch.uint8, device=dev, generator=g)
+            sfb = gplk.nvfp4_sf_bytes(n, n)
+            SFA = torch.full((sfb,), 0x38, dtype=torch.uint8, device=dev)
+            SFB = torch.full((sfb,), 0x38, dtype=torch.uint8, device=dev)
+            D = torch.empty(n, n, dtype=torch.bfloat16, device=dev)
+            al = torch.ones(1, device=dev)
+
+            def step():
+                gplk.gemm_nvfp4_tn(A, B, SFA, SFB, D, n, al, stream=stream)
+
+            dtype, workload = "e2m1", "NVFP4 E2M1 TN GEMM M=N=K=16384, UE4M3 per-16 scales, BF16 out"
+        launches_per_step = 1
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(dist.local)
+    dist.barrier()
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    sampler.stop()
+    ms = e0.elapsed_time(e1)
+    ms_max = dist.max(ms)
+    flops = 2.0 * n ** 3
+    # Kernel-only duration for the roofline: time the GEMM alone (no flush).
+    if w == "sgemm":
+        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        k0.record(stream)
+        for _ in range(args.steps):
+            gplk.sgemm(A, B, C, stream=stream)
+        k1.record(stream)
+        torch.cuda.synchronize()
+        kernel_s = k0.elapsed_time(k1) / 1e3 / args.steps
+    else:
+        kernel_s = ms / 1e3 / args.steps
+    achieved = flops / kernel_s / 1e12
+    value = dist.world * flops * args.steps / (ms_max / 1e3) / 1e12
+    peak = NOMINAL_TFLOPS[w]
+    return {
+        "metric": f"{w} TFLOP/s", "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": dist.world,
+        "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms_max / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype,
+        "data": "synthetic, seeded",
+        "config": {"workload": workload, "size": n,
+                   "l2": "256 MiB L2 flush per step" if w == "sgemm" else "operands larger than L2",
+                   "parallelism": f"replicas x{dist.world}"},
+        "roofline": {"bound": "tensor" if w != "sgemm" else "fp32-simt", "achieved": round(achieved, 1),
+                     "peak": round(peak, 1), "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                     "traffic": NCU_TRAFFIC[w], "peak_source": "nominal dense"},
+        "clocks": sampler.summary(),
+        "gpu_launches": args.steps * (1 if w != "sgemm" else 1),
+    }
+
+
+# ------------------------------------------------------------ reference arm
+
+def bench_reference(args, dist: Dist) -> dict | None:
+    if dist.rank != 0:
+        return None
+    sys.path.insert(0, str(REPO / "oracle"))
+    import numpy as np
+    import oracle
+
+    n = 1 << 28
+    b = oracle.uniform_f32(n, seed=101)
+    c = oracle.uniform_f32(n, seed=202)
+    a = np.empty_like(b)
+    th = oracle.max_threads()
+    for _ in range(max(args.warmup, 1)):
+        oracle.triad_into(a, b, c, TRIAD_S, th)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.triad_into(a, b, c, TRIAD_S, th)
+    el = time.perf_counter() - t0
+    value = 12 * n * args.steps / el / 1e9
+    sample = f"each step: one host triad over 3 x 2^28 FP32 (3 GiB) of the 3 x 2^30 workload"
+    return {
+        "impl": "reference", "metric": "memstream triad GB/s", "value": round(value, 2), "unit": "GB/s",
+        "n_gpus": dist.world, "steps": args.steps, "warmup": max(args.warmup, 1),
+        "ms_per_step": round(el * 1e3 / args.steps, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic: b, c ~ U[0,1) seeded, s = 3.0",
+        "config": {"workload": "memstream STREAM triad a = b + 3.0*c, FP32, 3 x 2^30 elements (4 GiB each)",
+                   "sampled_elements_per_step": n},
+        "cpu_baseline": {"value": round(value, 2), "unit": "GB/s", "cores": th, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 2), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        # Host-only arm: no process group; under torchrun only rank 0 works.
+        class _Ranks:
+            rank = int(os.environ.get("RANK", "0"))
+            world = int(os.environ.get("WORLD_SIZE", "1"))
+
+        line = bench_reference(args, _Ranks())
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+
+    dist = Dist(args.gpus)
+    try:
+        if args.workload == "memstream":
+            line = bench_memstream(args, dist)
+        elif args.workload in ("sgemm", "fp8", "nvfp4"):
+            line = bench_gemm(args, dist)
+        else:
+            raise SystemExit("powervirus: not a bench.py workload yet")
+        if dist.rank == 0 and dist.world == 1 and not args.no_cpu and args.workload == "memstream":
+            line["cpu_baseline"] = cpu_triad_gbps(args.cpu_seconds)
+        if dist.rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        dist.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,407 @@
+// gplk_gemm_tc.cu - tcgen05 GEMMs for the narrow formats of the GEMM ladder:
+//   FP8   E4M3 x E4M3, per-tensor FP32 scales           (kind::f8f6f4)
+//   NVFP4 E2M1 x E2M1, UE4M3 scale per 16 K-elements     (kind::mxf4nvf4.block16)
+// both with FP32 accumulation in TMEM and BF16 output, in cuBLASLt's TN
+// convention (A and B K-major, D column-major M x N).
+//
+// One persistent CTA per SM walks output tiles of 128 x 256 in a grouped
+// (L2-friendly) order. Warp roles:
+//   warp 0      TMA producer: 2-D tiled loads of A (128 rows) and B (256
+//               rows), 128 bytes of K per stage with 128-byte swizzle, into a
+//               STAGES-deep shared-memory ring; NVFP4 adds 1-D bulk copies of
+//               the stage's scale-factor blocks. No cluster multicast.
+//   warp 1      owns TMEM; one thread issues the MMAs (4 per stage: K = 32
+//               FP8 or 64 FP4 elements per instruction) and, for NVFP4,
+//               the shared->TMEM copies of the scale factors first.
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator, scale, BF16, global
+//               stores. Warp w reads TMEM lanes 32*(w%4)..+31 (= tile rows).
+// FP8 double-buffers the accumulator (2 x 256 TMEM columns) so the epilogue of
+// one tile overlaps the main loop of the next. NVFP4 needs TMEM for per-stage
+// scale factors, so it keeps one accumulator and drains it into registers
+// before storing, releasing TMEM early.
+// Every mbarrier wait is bounded; on timeout the kernel records
+// GPLK_STATUS_DEVICE_TIMEOUT, drains outstanding copies and MMAs, frees TMEM
+// and returns.
+#include "gplk_ptx.cuh"
+
+namespace gplk {
+namespace gemm_tc {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK_BYTES = 128;  // one 128-byte swizzle row of K per stage
+constexpr int A_STAGE = BM * BK_BYTES;   // 16 KiB
+constexpr int B_STAGE = BN * BK_BYTES;   // 32 KiB
+constexpr int SFA_STAGE = 4 * 512;       // 4 K-blocks of 128 rows x 4 scales
+constexpr int SFB_STAGE = 8 * 512;       // 2 row-halves x 4 K-blocks
+constexpr int kThreads = 192;
+constexpr int kGroupM = 8;               // tile raster group along M
+
+template <bool NVF4>
+struct Traits {
+    static constexpr int kStages = 4;
+    static constexpr int kStageBytes = A_STAGE + B_STAGE + (NVF4 ? SFA_STAGE + SFB_STAGE : 0);
+    static constexpr int kAccBufs = NVF4 ? 1 : 2;
+    static constexpr uint32_t kTmemCols = 512;
+    // TMEM column map. Accumulators first; NVFP4 scale factors after them,
+    // one 48-column slot per stage (16 for A, 32 for B).
+    static constexpr uint32_t kSfCol0 = 256;
+    static constexpr uint32_t kSfColsPerStage = 48;
+    static_assert(!NVF4 || kSfCol0 + kStages * kSfColsPerStage <= kTmemCols, "TMEM budget");
+};
+
+template <bool NVF4>
+struct __align__(1024) Smem {
+    uint8_t stage[Traits<NVF4>::kStages][Traits<NVF4>::kStageBytes];
+    uint64_t full[Traits<NVF4>::kStages];
+    uint64_t empty[Traits<NVF4>::kStages];
+    uint64_t acc_full[2];
+    uint64_t acc_empty[2];
+    uint64_t drain;
+    uint32_t tmem_base;
+    int abort;
+};
+
+struct Params {
+    uint16_t* D;
+    const uint8_t* sfa;  // NVFP4 only
+    const uint8_t* sfb;
+    const float* scale_a;  // FP8: per-tensor scales; NVFP4: scale_a = alpha
+    const float* scale_b;
+    int M, N, K;           // K in elements
+    int m_tiles, n_tiles, k_stages;
+    int sf_kblocks4;       // NVFP4: ceil(K / 64) = 512-byte blocks per 128 rows
+    int sf_row_blocks_b;   // NVFP4: ceil(N / 128) row blocks in SFB
+};
+
+__device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int& mt, int& nt) {
+    const int per_group = kGroupM * n_tiles;
+    const int group = t / per_group;
+    const int first_m = group * kGroupM;
+    const int gsize = min(m_tiles - first_m, kGroupM);
+    const int r = t % per_group;
+    mt = first_m + r % gsize;
+    nt = r / gsize;
+}
+
+template <bool NVF4>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const Params p) {
+    using TR = Traits<NVF4>;
+    constexpr int S = TR::kStages;
+    extern __shared__ uint8_t smem_raw[];
+    Smem<NVF4>& sm = *reinterpret_cast<Smem<NVF4>*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+
+    const uint32_t warp = warp_id_uniform();
+    const uint32_t lane = lane_id();
+    const int num_tiles = p.m_tiles * p.n_tiles;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i) {
+            mbar_init(&sm.full[i], 1);
+            mbar_init(&sm.empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&sm.acc_full[i], 1);
+            mbar_init(&sm.acc_empty[i], 4);
+        }
+        mbar_init(&sm.drain, 1);
+        sm.abort = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(&sm.tmem_base, TR::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = sm.tmem_base;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued_mask = 0, issued_parity = 0;  // for the abort drain
+            bool ok = true;
+            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+                int mt, nt;
+                tile_coords(t, p.m_tiles, p.n_tiles, mt, nt);
+                for (int kb = 0; kb < p.k_stages; ++kb) {
+                    if (!mbar_wait(&sm.empty[stage], phase ^ 1u, &sm.abort, 0x0201)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* st = sm.stage[stage];
+                    mbar_arrive_expect_tx(&sm.full[stage], TR::kStageBytes);
+                    tma_load_2d(st, &tmA, &sm.full[stage], kb * BK_BYTES, mt * BM);
+                    tma_load_2d(st + A_STAGE, &tmB, &sm.full[stage], kb * BK_BYTES, nt * BN);
+                    if constexpr (NVF4) {
+                        // A stage covers K-blocks 4*kb .. 4*kb+3 of row block mt:
+                        // 2 KiB contiguous. B covers two row blocks 2*nt, 2*nt+1.
+                        const size_t blk = (size_t)p.sf_kblocks4;
+                        const uint8_t* sa = p.sfa + ((size_t)mt * blk + (size_t)kb * 4) * 512;
+                        const uint8_t* sb0 = p.sfb + ((size_t)(2 * nt) * blk + (size_t)kb * 4) * 512;
+                        // A last tile with N % 256 <= 128 has no second row block;
+                        // its B rows are zero-filled by TMA and never stored, so
+                        // any in-bounds scale bytes will do.
+                        const int nb1 = (2 * nt + 1 < p.sf_row_blocks_b) ? 2 * nt + 1 : 2 * nt;
+                        const uint8_t* sb1 = p.sfb + ((size_t)nb1 * blk + (size_t)kb * 4) * 512;
+                        uint8_t* dsf = st + A_STAGE + B_STAGE;
+                        bulk_load(dsf, sa, SFA_STAGE, &sm.full[stage]);
+                        bulk_load(dsf + SFA_STAGE, sb0, SFB_STAGE / 2, &sm.full[stage]);
+                        bulk_load(dsf + SFA_STAGE + SFB_STAGE / 2, sb1, SFB_STAGE / 2, &sm.full[stage]);
+                    }
+                    issued_mask |= 1u << stage;
+                    issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (!ok || sm.abort) {
+                // Drain: every issued copy must land before the block exits.
+                int dummy = 0;
+                for (int s2 = 0; s2 < S; ++s2)
+                    if (issued_mask & (1u << s2))
+                        mbar_wait(&sm.full[s2], (issued_parity >> s2) & 1u, &dummy, 0x0202,
+                                  100000000ull);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = NVF4 ? idesc_nvf4(BM, BN) : idesc_e4m3_f32(BM, BN);
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+                if (!mbar_wait(&sm.acc_empty[acc], acc_phase ^ 1u, &sm.abort, 0x0211)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem + (uint32_t)acc * 256u;
+                for (int kb = 0; kb < p.k_stages; ++kb) {
+                    if (!mbar_wait(&sm.full[stage], phase, &sm.abort, 0x0212)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(sm.stage[stage]);
+                    const uint32_t b_addr = a_addr + A_STAGE;
+                    if constexpr (NVF4) {
+                        const uint32_t sf_addr = b_addr + B_STAGE;
+                        const uint32_t sf_col = tmem + TR::kSfCol0 + (uint32_t)stage * TR::kSfColsPerStage;
+                        // A: K-block j -> 4 columns at sf_col + 4j.
+                        // B: K-block j, row half h -> 4 columns at sf_col + 16 + 8j + 4h.
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            tmem_cp_32x128b_warpx4(sf_col + 4 * j, smem_desc(sf_addr + 512 * j, 0, 128, 0));
+#pragma unroll
+                            for (int h = 0; h < 2; ++h)
+                                tmem_cp_32x128b_warpx4(
+                                    sf_col + 16 + 8 * j + 4 * h,
+                                    smem_desc(sf_addr + SFA_STAGE + h * (SFB_STAGE / 2) + 512 * j, 0, 128, 0));
+                        }
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            mma_nvf4(d_tmem, desc_kmajor_sw128(a_addr + 32 * j),
+                                     desc_kmajor_sw128(b_addr + 32 * j), idesc, sf_col + 4 * j,
+                                     sf_col + 16 + 8 * j, (kb | j) != 0);
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            mma_f8f6f4(d_tmem, desc_kmajor_sw128(a_addr + 32 * j),
+                                       desc_kmajor_sw128(b_addr + 32 * j), idesc, (kb | j) != 0);
+                        }
+                    }
+                    tc_commit(&sm.empty[stage]);
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                tc_commit(&sm.acc_full[acc]);
+                if (++acc == TR::kAccBufs) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+            // Every MMA issued by this thread completes before TMEM is freed.
+            tc_commit(&sm.drain);
+            int dummy = 0;
+            mbar_wait(&sm.drain, 0, &dummy, 0x0213, 100000000ull);
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const uint32_t quarter = warp & 3u;  // TMEM lanes 32*quarter .. +31
+        const int row_in_tile = (int)(quarter * 32 + lane);
+        const float scale = NVF4 ? __ldg(p.scale_a) : __ldg(p.scale_a) * __ldg(p.scale_b);
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+            int mt, nt;
+            tile_coords(t, p.m_tiles, p.n_tiles, mt, nt);
+            if (!mbar_wait(&sm.acc_full[acc], acc_phase, &sm.abort, 0x0221)) break;
+            tc_fence_after();
+            const int m = mt * BM + row_in_tile;
+            const int n_base = nt * BN;
+            const uint32_t t_addr = tmem + ((quarter * 32u) << 16) + (uint32_t)acc * 256u;
+            uint16_t* drow = p.D + m;  // column-major: D[m + n * M]
+            const size_t ldd = (size_t)p.M;
+            if constexpr (NVF4) {
+                // Drain all 256 columns to registers, release TMEM, then store.
+                uint32_t packed[128];
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(t_addr + 32u * c, r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        packed[c * 16 + j] = pack_bf16x2(__uint_as_float(r[2 * j]) * scale,
+                                                         __uint_as_float(r[2 * j + 1]) * scale);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sm.acc_empty[acc]);
+                if (m < p.M) {
+#pragma unroll
+                    for (int j = 0; j < 128; ++j) {
+                        const int n = n_base + 2 * j;
+                        if (n < p.N) drow[(size_t)n * ldd] = (uint16_t)(packed[j] & 0xFFFFu);
+                        if (n + 1 < p.N) drow[(size_t)(n + 1) * ldd] = (uint16_t)(packed[j] >> 16);
+                    }
+                }
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < 8; ++c) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(t_addr + 32u * c, r);
+                    tmem_ld_wait();
+                    if (m < p.M) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 2) {
+                            const uint32_t v = pack_bf16x2(__uint_as_float(r[j]) * scale,
+                                                           __uint_as_float(r[j + 1]) * scale);
+                            const int n = n_base + 32 * c + j;
+                            if (n < p.N) drow[(size_t)n * ldd] = (uint16_t)(v & 0xFFFFu);
+                            if (n + 1 < p.N) drow[(size_t)(n + 1) * ldd] = (uint16_t)(v >> 16);
+                        }
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sm.acc_empty[acc]);
+            }
+            if (++acc == TR::kAccBufs) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, TR::kTmemCols);
+    }
+}
+
+template <bool NVF4>
+static int smem_bytes() {
+    return (int)sizeof(Smem<NVF4>) + 1024;
+}
+
+template <bool NVF4>
+static int launch(const uint8_t* A, const uint8_t* B, const uint8_t* SFA, const uint8_t* SFB,
+                  uint16_t* D, int M, int N, int K, const float* sa, const float* sb,
+                  cudaStream_t stream) {
+    DeviceInfo d;
+    int st = require_sm100(&d);
+    if (st != GPLK_STATUS_OK) return st;
+    const int smem = smem_bytes<NVF4>();
+    if (smem > d.max_smem_optin) return GPLK_STATUS_UNSUPPORTED;
+    static thread_local uint64_t configured = 0;  // bit per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(configured & (1ull << dev))) {
+        if (cudaFuncSetAttribute(gemm_tc_kernel<NVF4>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+            cudaSuccess)
+            return GPLK_STATUS_LAUNCH_FAIL;
+        configured |= 1ull << dev;
+    }
+    // Operand row length in bytes: K for E4M3, K/2 for packed E2M1.
+    const uint64_t row_bytes = NVF4 ? (uint64_t)K / 2 : (uint64_t)K;
+    CUtensorMap tmA, tmB;
+    st = encode_tmap_2d_u8(&tmA, A, row_bytes, (uint64_t)M, row_bytes, BK_BYTES, BM);
+    if (st != GPLK_STATUS_OK) return st;
+    st = encode_tmap_2d_u8(&tmB, B, row_bytes, (uint64_t)N, row_bytes, BK_BYTES, BN);
+    if (st != GPLK_STATUS_OK) return st;
+
+    Params p;
+    p.D = D;
+    p.sfa = SFA;
+    p.sfb = SFB;
+    p.scale_a = sa;
+    p.scale_b = sb;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.m_tiles = (M + BM - 1) / BM;
+    p.n_tiles = (N + BN - 1) / BN;
+    p.k_stages = (int)((row_bytes + BK_BYTES - 1) / BK_BYTES);
+    p.sf_kblocks4 = (K + 63) / 64;
+    p.sf_row_blocks_b = (N + 127) / 128;
+    const int tiles = p.m_tiles * p.n_tiles;
+    const int grid = tiles < d.sm_count ? tiles : d.sm_count;
+    gemm_tc_kernel<NVF4><<<grid, kThreads, smem, stream>>>(tmA, tmB, p);
+    return launch_status(cudaGetLastError());
+}
+
+}  // namespace gemm_tc
+}  // namespace gplk
+
+extern "C" int gplk_gemm_fp8_tn(const uint8_t* A, const uint8_t* B, uint16_t* D, int M, int N, int K,
+                                const float* scale_a, const float* scale_b, cudaStream_t stream) {
+    using namespace gplk;
+    if (M < 0 || N < 0 || K < 0) return GPLK_STATUS_BAD_ARG;
+    if (M == 0 || N == 0) return GPLK_STATUS_OK;
+    if (K == 0 || K % 16 != 0) return GPLK_STATUS_BAD_ARG;
+    if (!A || !B || !D || !scale_a || !scale_b) return GPLK_STATUS_BAD_ARG;
+    if (!aligned16(A) || !aligned16(B)) return GPLK_STATUS_BAD_ARG;
+    return gemm_tc::launch<false>(A, B, nullptr, nullptr, D, M, N, K, scale_a, scale_b, stream);
+}
+
+extern "C" size_t gplk_nvfp4_sf_bytes(int rows, int k) {
+    if (rows <= 0 || k <= 0) return 0;
+    const size_t row_blocks = ((size_t)rows + 127) / 128;
+    const size_t k_blocks4 = ((size_t)k + 63) / 64;
+    return row_blocks * k_blocks4 * 512;
+}
+
+extern "C" int gplk_gemm_nvfp4_tn(const uint8_t* A, const uint8_t* B, const uint8_t* SFA,
+                                  const uint8_t* SFB, uint16_t* D, int M, int N, int K,
+                                  const float* alpha, cudaStream_t stream) {
+    using namespace gplk;
+    if (M < 0 || N < 0 || K < 0) return GPLK_STATUS_BAD_ARG;
+    if (M == 0 || N == 0) return GPLK_STATUS_OK;
+    if (K == 0 || K % 256 != 0) return GPLK_STATUS_BAD_ARG;
+    if (!A || !B || !SFA || !SFB || !D || !alpha) return GPLK_STATUS_BAD_ARG;
+    if (!aligned16(A) || !aligned16(B) || !aligned16(SFA) || !aligned16(SFB)) return GPLK_STATUS_BAD_ARG;
+    return gemm_tc::launch<true>(A, B, SFA, SFB, D, M, N, K, alpha, alpha, stream);
+}

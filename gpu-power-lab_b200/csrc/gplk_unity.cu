@@ -1,0 +1,7 @@
+// gplk_unity.cu - the single translation unit of libgplk.so. Kernels share
+// the device status word in gplk_core.cu, so they are compiled together.
+#include "gplk_core.cu"
+#include "gplk_memstream.cu"
+#include "gplk_sgemm.cu"
+#include "gplk_gemm_tc.cu"
+#include "gplk_powervirus.cu"

@@ -1,0 +1,161 @@
+/*
+ * gplk.h - C ABI of libgplk, the B200 (sm_100a) kernel library behind the
+ * gpu-power-lab load generators.
+ *
+ * Every entry point:
+ *   - takes plain device pointers, sizes and a CUDA stream;
+ *   - allocates nothing and is stream-ordered (asynchronous: a device fault
+ *     or a device-side wait timeout shows up at the caller's next sync and
+ *     in gplk_status_read);
+ *   - returns a gplk_status code synchronously from argument and launch
+ *     checks.
+ *
+ * The reference path each launcher replaces is cited beside it
+ * (paths relative to the gpu-power-lab source tree).
+ */
+#ifndef GPLK_H
+#define GPLK_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    GPLK_STATUS_OK = 0,
+    GPLK_STATUS_BAD_ARG = 1,        /* a size, alignment or pointer check failed */
+    GPLK_STATUS_LAUNCH_FAIL = 2,    /* cudaLaunch / attribute call failed */
+    GPLK_STATUS_DEVICE_TIMEOUT = 3, /* a bounded device-side wait ran out */
+    GPLK_STATUS_UNSUPPORTED = 4,    /* device is not sm_100 or lacks a feature */
+    GPLK_STATUS_CUDA_ERROR = 5      /* any other CUDA runtime error */
+} gplk_status;
+
+/* Human-readable name of a gplk_status value (static storage). */
+const char *gplk_status_string(int status);
+
+/* ABI version: bumped when a signature or a data layout changes. */
+int gplk_abi_version(void);
+
+/* Reads the device status word of the current device (first error recorded
+ * by any gplk kernel since the last clear) and the site that recorded it.
+ * Synchronises the current device. If clear != 0 the word is reset to OK. */
+int gplk_status_read(int *code, int *site, int clear);
+
+/* ------------------------------------------------------------ memstream
+ * STREAM triad a[i] = b[i] + s * c[i] in FP32, computed as one fused
+ * multiply-add fmaf(s, c[i], b[i]) per element, so the result is bit-exact
+ * against a host loop that calls fmaf.
+ * Replaces stream_triad_kernel, runner/src/workload_memstream.cu:43-54
+ * (launched at :102, :117, :140; its arrays are C = A + scalar * B).
+ * a may not overlap b or c. n may be any size, including 0. */
+int gplk_triad_f32(float *a, const float *b, const float *c, float s, size_t n,
+                   cudaStream_t stream);
+
+/* Same triad, with the operands staged through shared memory by 1-D TMA bulk
+ * copies (cp.async.bulk) and the result written back by bulk stores.
+ * Requires a, b, c 16-byte aligned. */
+int gplk_triad_f32_bulk(float *a, const float *b, const float *c, float s, size_t n,
+                        cudaStream_t stream);
+
+/* dst[i] = src[i], FP32, 128-bit vectorised (the STREAM "copy" kernel). */
+int gplk_copy_f32(float *dst, const float *src, size_t n, cudaStream_t stream);
+
+/* ------------------------------------------------------------ SGEMM
+ * C = A * B in true FP32 (SIMT FFMA, no TF32), row-major:
+ * A is M x K (leading dimension lda), B is K x N (ldb), C is M x N (ldc).
+ * Replaces cublasGemmEx with CUBLAS_COMPUTE_32F / CUBLAS_DEFAULT_MATH,
+ * runner/src/workload_gemm.c:155-163, :174-179, :199-204 (column-major
+ * C = A * B there, which is the row-major product C^T = B^T * A^T here). */
+int gplk_sgemm_f32(const float *A, const float *B, float *C, int M, int N, int K, int lda,
+                   int ldb, int ldc, cudaStream_t stream);
+
+/* ------------------------------------------------------------ FP8 GEMM
+ * D = (*scale_a) * (*scale_b) * (A^T * B) with E4M3 operands, FP32
+ * accumulation and BF16 output, in cuBLASLt's TN convention:
+ *   A: K x M column-major (each of the M rows holds K contiguous bytes),
+ *   B: K x N column-major (each of the N columns holds K contiguous bytes),
+ *   D: M x N column-major BF16 (ld = M).
+ * scale_a / scale_b are device pointers to one FP32 each (per-tensor scales).
+ * Replaces gpl_lt_enqueue's cublasLtMatmul for GPL_PREC_FP8,
+ * runner/src/gemm_lt.cu:164-179 with the descriptor of :98-132.
+ * Requires K % 16 == 0 and 16-byte aligned A and B; M and N are free. */
+int gplk_gemm_fp8_tn(const uint8_t *A, const uint8_t *B, uint16_t *D, int M, int N, int K,
+                     const float *scale_a, const float *scale_b, cudaStream_t stream);
+
+/* ------------------------------------------------------------ NVFP4 GEMM
+ * D = (*alpha) * sum_k (sfa[m, k/16] * a[m, k]) * (sfb[n, k/16] * b[n, k])
+ * with E2M1 operands packed two per byte (element 2j in the low nibble of
+ * byte j), one UE4M3 scale per 16 consecutive K-elements, FP32 accumulation
+ * and BF16 output. A and B are K-major as for the FP8 GEMM (rows of K/2
+ * bytes); D is M x N column-major BF16.
+ * SFA / SFB use cuBLASLt's CUBLASLT_MATMUL_MATRIX_SCALE_VEC16_UE4M3 layout:
+ * 128-row x 4-scale blocks of 512 bytes, block (r/128, kb/4) at byte offset
+ * ((r/128) * ceil(K/64) + kb/4) * 512, and inside a block
+ * (r % 32) * 16 + ((r % 128) / 32) * 4 + kb % 4. Row counts are padded to a
+ * multiple of 128 and scale columns to a multiple of 4.
+ * alpha is a device pointer to the FP32 product of the per-tensor scales.
+ * This is the NVFP4 path that runner/src/gemm_lt.cu:76-82 tries to reach
+ * (GPL_PREC_FP4) without block scales. Requires K % 256 == 0. */
+int gplk_gemm_nvfp4_tn(const uint8_t *A, const uint8_t *B, const uint8_t *SFA,
+                       const uint8_t *SFB, uint16_t *D, int M, int N, int K, const float *alpha,
+                       cudaStream_t stream);
+
+/* Bytes of one scale-factor array in the layout above, for `rows` rows and
+ * a K extent of k elements. */
+size_t gplk_nvfp4_sf_bytes(int rows, int k);
+
+/* ------------------------------------------------------------ powervirus */
+
+#define GPLK_PV_ROLE_TENSOR 0  /* tcgen05 FP8 MMA into TMEM on smem-resident tiles */
+#define GPLK_PV_ROLE_FMA 1     /* dependent FP32 FFMA chains */
+#define GPLK_PV_ROLE_DRAM 2    /* HBM streaming by TMA bulk loads */
+#define GPLK_PV_ROLE_SFU 3     /* transcendentals */
+#define GPLK_PV_ROLE_INT32 4   /* integer multiply-add chains */
+#define GPLK_PV_ROLE_SMEM 5    /* shared-memory read/write traffic */
+#define GPLK_PV_ROLE_L2 6      /* L2-resident streaming */
+#define GPLK_PV_ROLE_ATOMIC 7  /* atomics resolved in L2 */
+#define GPLK_PV_ROLE_COUNT 8
+#define GPLK_PV_ROLE_SLOTS 64  /* warp-slot map size */
+
+typedef struct {
+    const unsigned char *role_map; /* device, GPLK_PV_ROLE_SLOTS entries */
+    const float *stream_buf;       /* device, HBM streaming source */
+    size_t stream_bytes;           /* multiple of 16, >= 64 KiB */
+    float *sink;                   /* device, 1 + 1024 floats (atomic targets) */
+    float *verify_out;             /* device or NULL: one 32-bit word per thread (see below) */
+    const uint8_t *mma_a;          /* device or NULL: 128 x 128 E4M3 tile, K-major */
+    const uint8_t *mma_b;          /* device or NULL: 256 x 128 E4M3 tile, K-major */
+    float *mma_out;                /* device or NULL: 128 x 256 F32 accumulator dump */
+    int blocks;                    /* grid size; 0 = one block per SM */
+    int inner;                     /* iterations of each role per launch */
+} gplk_pv_cfg;
+
+/* One launch of the mixed-unit power kernel.
+ * Replaces gpl_powervirus_kernel, runner/src/workload_powervirus.cu:100-249.
+ * Blocks of gplk_pv_block_threads() threads (32 warps); warp w of block b
+ * takes the role role_map[(2 * w + b % 2) % 64], so every block carries the
+ * whole mix. With verify_out set, thread t of global warp g writes its role's
+ * final 32-bit value (FMA chain sum bits, LCG xor, ...) to
+ * verify_out[g * 32 + t] for bit-exact host checks; with mma_out set, block 0
+ * dumps its 128 x 256 TMEM accumulator (row-major FP32) after `inner` tile
+ * MMAs (each tile = A(128x128) x B(256x128)^T over K = 128). */
+int gplk_powervirus_launch(const gplk_pv_cfg *cfg, cudaStream_t stream);
+
+/* Largest-remainder apportionment of GPLK_PV_ROLE_SLOTS warp slots over the
+ * eight role weights (runner/src/workload_powervirus.cu:414-454): a role
+ * with a non-zero weight always gets at least one slot. Writes map[64] and
+ * counts[8]. */
+void gplk_pv_build_role_map(const int weights[GPLK_PV_ROLE_COUNT], unsigned char *map,
+                            int *counts);
+
+/* Threads per powervirus block (warps = value / 32). */
+int gplk_pv_block_threads(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GPLK_H */

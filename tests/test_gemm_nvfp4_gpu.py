@@ -1,0 +1,69 @@
+"""NVFP4 block-scaled GEMM (tcgen05 kind::mxf4nvf4, UE4M3 scale per 16
+K-elements) against the double-accumulated oracle on the same quantised
+operands and scale bytes. Bar: relative Frobenius error <= 1e-2."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2
+
+
+def _rel_fro(got, want):
+    got = np.asarray(got, np.float64)
+    return float(np.linalg.norm(got - want) / max(np.linalg.norm(want), 1e-300))
+
+
+def _operands(oracle, M, N, K, seed):
+    a = oracle.normal_f32(M * K, seed).reshape(M, K)
+    b = oracle.normal_f32(N * K, seed + 1).reshape(N, K)
+    pa, sfa, ga = oracle.quantize_nvfp4(a)
+    pb, sfb, gb = oracle.quantize_nvfp4(b)
+    return pa, sfa, pb, sfb, ga * gb
+
+
+def _run(gplk, pa, sfa, pb, sfb, alpha, K, cuda):
+    import torch
+
+    M, N = pa.shape[0], pb.shape[0]
+    t = lambda x: torch.from_numpy(x).to(cuda)
+    D = torch.full((N, M), float("nan"), dtype=torch.bfloat16, device=cuda)
+    al = torch.tensor([alpha], dtype=torch.float32, device=cuda)
+    gplk.gemm_nvfp4_tn(t(pa), t(pb), t(sfa), t(sfb), D, K, al)
+    torch.cuda.synchronize()
+    return D.float().cpu().numpy()
+
+
+@pytest.mark.parametrize("mnk", [(128, 256, 256), (256, 256, 512), (512, 768, 1024), (128, 384, 512),
+                                 (200, 300, 256), (1024, 1024, 2048)])
+def test_nvfp4_full_vs_oracle(mnk, gplk, oracle, cuda):
+    M, N, K = mnk
+    pa, sfa, pb, sfb, alpha = _operands(oracle, M, N, K, seed=M + 3 * N)
+    got = _run(gplk, pa, sfa, pb, sfb, alpha, K, cuda)
+    want = oracle.gemm_nvfp4_tn(pa, pb, sfa, sfb, K, alpha)
+    assert np.isfinite(got).all()
+    assert _rel_fro(got, want) <= TOL, mnk
+    bf = oracle.bf16_round(want.astype(np.float32))
+    assert np.max(np.abs(got - bf)) <= 2 ** -7 * np.max(np.abs(want)) + 1e-6
+
+
+@pytest.mark.parametrize("n", [2048, 4096, 8192, 16384])
+def test_nvfp4_ladder_sampled_vs_oracle(n, gplk, oracle, cuda):
+    pa, sfa, pb, sfb, alpha = _operands(oracle, n, n, n, seed=n)
+    got = _run(gplk, pa, sfa, pb, sfb, alpha, n, cuda)
+    rng = np.random.default_rng(n)
+    pairs = np.stack([rng.integers(0, n, 2048), rng.integers(0, n, 2048)], axis=1)
+    want = oracle.gemm_nvfp4_tn(pa, pb, sfa, sfb, n, alpha, pairs)
+    assert _rel_fro(got[pairs[:, 1], pairs[:, 0]], want) <= TOL
+
+
+def test_nvfp4_rejects_bad_k(gplk, cuda):
+    import torch
+
+    A = torch.zeros(128, 64, dtype=torch.uint8, device=cuda)  # K = 128
+    sf = torch.zeros(4096, dtype=torch.uint8, device=cuda)
+    D = torch.empty(128, 128, dtype=torch.bfloat16, device=cuda)
+    al = torch.ones(1, device=cuda)
+    with pytest.raises(gplk.GplkError):
+        gplk.gemm_nvfp4_tn(A, A, sf, sf, D, 128, al)

@@ -1,0 +1,86 @@
+"""FP32 SGEMM on the GPU against the double-accumulated host triple loop
+(tolerance 1e-5 relative, Frobenius and max-norm)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-5
+
+
+def _rel_fro(got, want):
+    return float(np.linalg.norm(got.astype(np.float64) - want) / max(np.linalg.norm(want), 1e-300))
+
+
+def _run(gplk, A, B, cuda):
+    import torch
+
+    tA, tB = torch.from_numpy(A).to(cuda), torch.from_numpy(B).to(cuda)
+    C = torch.full((A.shape[0], B.shape[1]), float("nan"), device=cuda)
+    gplk.sgemm(tA, tB, C)
+    torch.cuda.synchronize()
+    return C.cpu().numpy()
+
+
+def test_sgemm_1024_seed0(gplk, oracle, cuda):
+    n = 1024
+    A = oracle.uniform_f32(n * n, seed=0, lo=-1.0, hi=1.0).reshape(n, n)
+    B = oracle.uniform_f32(n * n, seed=1, lo=-1.0, hi=1.0).reshape(n, n)
+    got = _run(gplk, A, B, cuda)
+    want = oracle.sgemm_f64acc(A, B)
+    assert _rel_fro(got, want) <= TOL
+    assert float(np.max(np.abs(got - want))) <= TOL * float(np.max(np.abs(want)))
+
+
+@pytest.mark.parametrize("mnk", [(1, 1, 1), (33, 17, 5), (100, 130, 257), (257, 129, 1000),
+                                 (64, 64, 16), (128, 256, 64), (2048, 512, 300), (3000, 2000, 128)])
+def test_sgemm_shapes(mnk, gplk, oracle, cuda):
+    M, N, K = mnk
+    A = oracle.uniform_f32(M * K, seed=M, lo=-1.0, hi=1.0).reshape(M, K)
+    B = oracle.uniform_f32(K * N, seed=N + 7, lo=-1.0, hi=1.0).reshape(K, N)
+    got = _run(gplk, A, B, cuda)
+    want = oracle.sgemm_f64acc(A, B)
+    assert _rel_fro(got, want) <= TOL, mnk
+
+
+def test_sgemm_strided_views(gplk, oracle, cuda):
+    import torch
+
+    M, N, K = 200, 120, 96
+    big = torch.from_numpy(oracle.uniform_f32(M * (K + 8), 3, -1, 1).reshape(M, K + 8)).to(cuda)
+    A = big[:, :K]  # lda = K + 8
+    B = torch.from_numpy(oracle.uniform_f32(K * N, 4, -1, 1).reshape(K, N)).to(cuda)
+    C = torch.empty(M, N, device=cuda)
+    gplk.sgemm(A, B, C)
+    torch.cuda.synchronize()
+    want = oracle.sgemm_f64acc(np.ascontiguousarray(A.cpu().numpy()), B.cpu().numpy())
+    assert _rel_fro(C.cpu().numpy(), want) <= TOL
+
+
+def test_sgemm_k_zero_writes_zeros(gplk, cuda):
+    import torch
+
+    A = torch.empty(8, 0, device=cuda)
+    B = torch.empty(0, 8, device=cuda)
+    C = torch.full((8, 8), 5.0, device=cuda)
+    gplk.sgemm(A, B, C)
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(C) == 0
+
+
+def test_sgemm_matches_cublas_fp32(gplk, oracle, cuda):
+    """Cross-check against cuBLAS in true FP32 (TF32 off), the library the
+    reference's sgemm rung calls."""
+    import torch
+
+    torch.backends.cuda.matmul.allow_tf32 = False
+    n = 1024
+    A = torch.from_numpy(oracle.uniform_f32(n * n, 0, -1, 1).reshape(n, n)).to(cuda)
+    B = torch.from_numpy(oracle.uniform_f32(n * n, 1, -1, 1).reshape(n, n)).to(cuda)
+    C = torch.empty(n, n, device=cuda)
+    gplk.sgemm(A, B, C)
+    ref = A @ B
+    torch.cuda.synchronize()
+    rel = (torch.linalg.norm((C - ref).double()) / torch.linalg.norm(ref.double())).item()
+    assert rel <= TOL
