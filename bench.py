@@ -61,6 +61,8 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--elements", type=int, default=TRIAD_N,
+                    help="memstream array length (smaller cases are for profiling only)")
     return ap.parse_args()
 
 
@@ -233,9 +235,11 @@ def bench_memstream(args, dist: Dist) -> dict:
     gplk.lib()
     g = torch.Generator(device=dev)
     g.manual_seed(1234 + dist.rank)
-    b = torch.rand(TRIAD_N, device=dev, generator=g)
-    c = torch.rand(TRIAD_N, device=dev, generator=g)
-    a = torch.empty(TRIAD_N, device=dev)
+    n = args.elements
+    nbytes = 12 * n
+    b = torch.rand(n, device=dev, generator=g)
+    c = torch.rand(n, device=dev, generator=g)
+    a = torch.empty(n, device=dev)
     stream = torch.cuda.current_stream(dev)
     bulk = args.kernel == "bulk"
 
@@ -264,13 +268,17 @@ def bench_memstream(args, dist: Dist) -> dict:
         raise RuntimeError(f"device status {code} at {site:#x}")
 
     per_launch_s = ms / 1e3 / args.steps
-    achieved = TRIAD_BYTES / per_launch_s / 1e9
+    achieved = nbytes / per_launch_s / 1e9
     peaks = measured_peaks()
-    value = dist.world * TRIAD_BYTES * args.steps / (ms_max / 1e3) / 1e9
+    value = dist.world * nbytes * args.steps / (ms_max / 1e3) / 1e9
 
     e2e = None
     if not args.no_e2e:
         e2e = memstream_e2e(a, b, c, stream, bulk, dist, steps=3)
+    if n != TRIAD_N:
+        workload = f"memstream STREAM triad a = b + 3.0*c, FP32, 3 x {n} elements (profiling case)"
+    else:
+        workload = "memstream STREAM triad a = b + 3.0*c, FP32, 3 x 2^30 elements (4 GiB each)"
 
     traffic = NCU_TRAFFIC["memstream"]
     out = {
@@ -286,15 +294,15 @@ def bench_memstream(args, dist: Dist) -> dict:
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic: b, c ~ U[0,1) from torch's seeded generator, s = 3.0",
-        "config": {"workload": "memstream STREAM triad a = b + 3.0*c, FP32, 3 x 2^30 elements (4 GiB each)",
-                   "elements": TRIAD_N, "bytes_per_step_per_gpu": TRIAD_BYTES,
+        "config": {"workload": workload,
+                   "elements": n, "bytes_per_step_per_gpu": nbytes,
                    "kernel": "triad_bulk" if bulk else "triad_vec4",
                    "l2": "inputs (12 GiB per step) larger than the 126 MB L2; no flush",
                    "parallelism": f"replicas x{dist.world} (the workload does not shard)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
                      "peak_source": f"{peaks['_source']} hbm_gbs (burst copy)",
-                     "algorithmic_bytes_per_launch": TRIAD_BYTES},
+                     "algorithmic_bytes_per_launch": nbytes},
         "clocks": sampler.summary(),
         "gpu_launches": args.steps,
     }
@@ -309,9 +317,10 @@ def memstream_e2e(a, b, c, stream, bulk, dist: Dist, steps: int) -> dict:
     import torch
     import gplk
 
-    hb = torch.empty(TRIAD_N, dtype=torch.float32, pin_memory=True)
-    hc = torch.empty(TRIAD_N, dtype=torch.float32, pin_memory=True)
-    ha = torch.empty(TRIAD_N, dtype=torch.float32, pin_memory=True)
+    n = b.numel()
+    hb = torch.empty(n, dtype=torch.float32, pin_memory=True)
+    hc = torch.empty(n, dtype=torch.float32, pin_memory=True)
+    ha = torch.empty(n, dtype=torch.float32, pin_memory=True)
     hb.copy_(b, non_blocking=False)
     hc.copy_(c, non_blocking=False)
 
@@ -331,9 +340,9 @@ def memstream_e2e(a, b, c, stream, bulk, dist: Dist, steps: int) -> dict:
     e1.record(stream)
     torch.cuda.synchronize()
     ms = dist.max(e0.elapsed_time(e1))
-    value = dist.world * TRIAD_BYTES * steps / (ms / 1e3) / 1e9
-    return {"value": round(value, 2), "unit": "GB/s", "h2d_bytes_per_step": 8 * TRIAD_N,
-            "d2h_bytes_per_step": 4 * TRIAD_N, "steps": steps,
+    value = dist.world * 12 * n * steps / (ms / 1e3) / 1e9
+    return {"value": round(value, 2), "unit": "GB/s", "h2d_bytes_per_step": 8 * n,
+            "d2h_bytes_per_step": 4 * n, "steps": steps,
             "note": "pinned host b, c -> device, triad, device a -> pinned host, per step"}
 
 

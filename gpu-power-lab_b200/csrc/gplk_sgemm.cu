@@ -218,7 +218,7 @@ extern "C" int gplk_sgemm_f32(const float* A, const float* B, float* C, int M, i
     using namespace gplk;
     if (M < 0 || N < 0 || K < 0) return GPLK_STATUS_BAD_ARG;
     if (M == 0 || N == 0) return GPLK_STATUS_OK;
-    if (!A || !B || !C) return GPLK_STATUS_BAD_ARG;
+    if (!C || (K > 0 && (!A || !B))) return GPLK_STATUS_BAD_ARG;  // K == 0: A, B unread
     if ((K > 0 && (lda < K || ldb < N)) || ldc < N) return GPLK_STATUS_BAD_ARG;
     DeviceInfo d;
     int st = current_device_info(&d);

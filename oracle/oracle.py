@@ -312,3 +312,25 @@ def ref_role_map(weights, tensor_cublas: bool = False) -> tuple[np.ndarray, np.n
 # Precision codes of the reference's gpl_prec_t (runner/src/args.h:31-40).
 PREC = {"fp32": 1, "tf32": 2, "fp16": 3, "bf16": 4, "fp8": 5, "fp64": 6, "int8": 7, "fp4": 8}
 OP = {"sgemm": 1, "fft": 2, "memstream": 3, "powervirus": 4, "observe": 5, "nccl": 6}
+
+
+# ------------------------------------------------------------ cuBLASLt NVFP4 harness
+
+LT_SO = HERE / "liboracle_lt.so"
+_lt = None
+
+
+def lt_lib() -> ctypes.CDLL:
+    """cuBLASLt NVFP4 GEMM with VEC16_UE4M3 block scales (oracle/lt_nvfp4.cu)."""
+    global _lt
+    if _lt is None:
+        if not LT_SO.exists():
+            build()
+        L = ctypes.CDLL(str(LT_SO))
+        L.oracle_lt_gemm_nvfp4_tn.restype = _i
+        L.oracle_lt_gemm_nvfp4_tn.argtypes = [_p, _p, _p, _p, _p, _i, _i, _i, _f, _p, _sz, _p]
+        L.oracle_lt_gemm_nvfp4_tn_timed.restype = _i
+        L.oracle_lt_gemm_nvfp4_tn_timed.argtypes = [_p, _p, _p, _p, _p, _i, _i, _i, _f, _p, _sz, _i, _p,
+                                                    ctypes.POINTER(_f)]
+        _lt = L
+    return _lt

@@ -1,0 +1,125 @@
+"""Times the reference's own GPU paths next to libgplk on the same box and
+prints one JSON object (not collected by pytest; run on a GPU):
+
+    python tests/perf_reference_kernels.py
+
+  memstream  stream_triad_kernel compiled from the reference source
+             (runner/src/workload_memstream.cu:43-54, its launch geometry)
+             vs gplk_triad_f32 / gplk_triad_f32_bulk, 3 x 2^30 FP32
+  sgemm      cuBLAS FP32 (TF32 off; the reference's cublasGemmEx
+             COMPUTE_32F) vs gplk_sgemm_f32, 1024^3
+  fp8        the reference's gemm_lt.cu cuBLASLt FP8 (gpl_lt_enqueue)
+             vs gplk_gemm_fp8_tn, 8192^3
+  nvfp4      cuBLASLt NVFP4 with VEC16_UE4M3 scales (oracle/lt_nvfp4.cu)
+             vs gplk_gemm_nvfp4_tn, 2048..16384
+"""
+from __future__ import annotations
+
+import ctypes
+import json
+import sys
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent.parent
+sys.path[:0] = [str(REPO / "gpu-power-lab_b200"), str(REPO / "oracle")]
+
+import torch  # noqa: E402
+
+import gplk  # noqa: E402
+import oracle  # noqa: E402
+
+
+def timed(fn, reps, warm=3):
+    s = torch.cuda.current_stream()
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(reps):
+        fn()
+    e1.record(s)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps  # ms
+
+
+def memstream(out):
+    n = 1 << 30
+    b = torch.rand(n, device="cuda")
+    c = torch.rand(n, device="cuda")
+    a = torch.empty(n, device="cuda")
+    L = oracle.ref_lib()
+    st = torch.cuda.current_stream().cuda_stream
+    gb = lambda ms: 12 * n / (ms / 1e3) / 1e9
+    out["memstream_GBps"] = {
+        "reference_stream_triad_kernel": gb(timed(lambda: L.ref_triad_launch(a.data_ptr(), b.data_ptr(), c.data_ptr(), 3.0, n, st), 100)),
+        "gplk_triad_vec4": gb(timed(lambda: gplk.triad(a, b, c, 3.0), 100)),
+        "gplk_triad_bulk": gb(timed(lambda: gplk.triad(a, b, c, 3.0, bulk=True), 100)),
+        "gplk_copy": 8 * n / (timed(lambda: gplk.copy(a, b), 100) / 1e3) / 1e9,
+        "torch_copy": 8 * n / (timed(lambda: a.copy_(b), 100) / 1e3) / 1e9,
+    }
+    del a, b, c
+
+
+def sgemm(out):
+    torch.backends.cuda.matmul.allow_tf32 = False
+    n = 1024
+    A = torch.rand(n, n, device="cuda") * 2 - 1
+    B = torch.rand(n, n, device="cuda") * 2 - 1
+    C = torch.empty(n, n, device="cuda")
+    tf = lambda ms: 2 * n ** 3 / (ms / 1e3) / 1e12
+    out["sgemm_1024_TFLOPs"] = {
+        "cublas_fp32": tf(timed(lambda: torch.matmul(A, B, out=C), 200)),
+        "gplk_sgemm": tf(timed(lambda: gplk.sgemm(A, B, C), 200)),
+    }
+
+
+def fp8(out):
+    n = 8192
+    L = oracle.ref_lib()
+    g = L.ref_lt_new()
+    st = torch.cuda.current_stream().cuda_stream
+    assert L.gpl_lt_init(g, oracle.PREC["fp8"], n, st) == 0
+    A = torch.randint(0, 0x7E, (n, n), dtype=torch.uint8, device="cuda")
+    B = torch.randint(0, 0x7E, (n, n), dtype=torch.uint8, device="cuda")
+    D = torch.empty(n, n, dtype=torch.bfloat16, device="cuda")
+    s = torch.ones(1, device="cuda")
+    tf = lambda ms: 2 * n ** 3 / (ms / 1e3) / 1e12
+    out["fp8_8192_TFLOPs"] = {
+        "reference_gemm_lt_cublaslt": tf(timed(lambda: L.gpl_lt_enqueue(g, 1), 50)),
+        "gplk_gemm_fp8_tn": tf(timed(lambda: gplk.gemm_fp8_tn(A, B, D, s, s), 50)),
+    }
+    L.gpl_lt_free(g)
+    L.ref_lt_delete(g)
+
+
+def nvfp4(out):
+    res = {}
+    for n in (2048, 4096, 8192, 16384):
+        A = torch.randint(0, 256, (n, n // 2), dtype=torch.uint8, device="cuda")
+        B = torch.randint(0, 256, (n, n // 2), dtype=torch.uint8, device="cuda")
+        sfb = gplk.nvfp4_sf_bytes(n, n)
+        SF = torch.full((sfb,), 0x38, dtype=torch.uint8, device="cuda")
+        D = torch.empty(n, n, dtype=torch.bfloat16, device="cuda")
+        al = torch.ones(1, device="cuda")
+        ws = torch.empty(32 << 20, dtype=torch.uint8, device="cuda")
+        reps = max(5, int(2e13 / (2 * n ** 3)))
+        ms = ctypes.c_float(0)
+        rc = oracle.lt_lib().oracle_lt_gemm_nvfp4_tn_timed(A.data_ptr(), B.data_ptr(), SF.data_ptr(), SF.data_ptr(),
+                                                           D.data_ptr(), n, n, n, 1.0, ws.data_ptr(), ws.numel(), reps,
+                                                           torch.cuda.current_stream().cuda_stream, ctypes.byref(ms))
+        tf = lambda m: 2 * n ** 3 / (m / 1e3) / 1e12
+        res[n] = {
+            "cublaslt_nvfp4": tf(ms.value / reps) if rc == 0 else f"rc={rc}",
+            "gplk_gemm_nvfp4_tn": tf(timed(lambda: gplk.gemm_nvfp4_tn(A, B, SF, SF, D, n, al), reps)),
+        }
+    out["nvfp4_TFLOPs"] = res
+
+
+if __name__ == "__main__":
+    which = sys.argv[1:] or ["memstream", "sgemm", "fp8", "nvfp4"]
+    out = {"device": torch.cuda.get_device_name()}
+    for w in which:
+        globals()[w](out)
+        torch.cuda.empty_cache()
+    print(json.dumps(out, indent=1, default=float))

@@ -67,3 +67,25 @@ def test_nvfp4_rejects_bad_k(gplk, cuda):
     al = torch.ones(1, device=cuda)
     with pytest.raises(gplk.GplkError):
         gplk.gemm_nvfp4_tn(A, A, sf, sf, D, 128, al)
+
+
+@pytest.mark.parametrize("n", [2048, 4096, 8192, 16384])
+def test_nvfp4_vs_cublaslt(n, gplk, oracle, cuda):
+    """The NVFP4 ladder against cuBLASLt's NVFP4 GEMM (VEC16_UE4M3 block
+    scales, the configuration runner/src/gemm_lt.cu lacks) on identical
+    operands and scale bytes: relative Frobenius error <= 1e-2 over all of D."""
+    import torch
+
+    pa, sfa, pb, sfb, alpha = _operands(oracle, n, n, n, seed=n + 1)
+    ours = _run(gplk, pa, sfa, pb, sfb, alpha, n, cuda)
+    t = lambda x: torch.from_numpy(x).to(cuda)
+    ref = torch.empty((n, n), dtype=torch.bfloat16, device=cuda)
+    ws = torch.empty(32 << 20, dtype=torch.uint8, device=cuda)
+    tA, tB, tSA, tSB = t(pa), t(pb), t(sfa), t(sfb)
+    rc = oracle.lt_lib().oracle_lt_gemm_nvfp4_tn(
+        tA.data_ptr(), tB.data_ptr(), tSA.data_ptr(), tSB.data_ptr(), ref.data_ptr(), n, n, n, alpha,
+        ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    ref = ref.float().cpu().numpy().astype(np.float64)
+    assert _rel_fro(ours, ref) <= TOL
