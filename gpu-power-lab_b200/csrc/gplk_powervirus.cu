@@ -208,7 +208,9 @@ __global__ void __launch_bounds__(kThreads, 1) pv_kernel(const Params p) {
             keep_bits = ok ? 0u : 1u;
         }
     } else if (role == GPLK_PV_ROLE_L2) {
-        const size_t win = kL2WindowBytes / sizeof(float4);
+        // The window never exceeds the buffer, so every read stays in bounds
+        // for the smallest buffer the launcher accepts (64 KiB).
+        const size_t win = min(kL2WindowBytes / sizeof(float4), p.stream_elems);
         const size_t base = ((size_t)blockIdx.x * 977) % (p.stream_elems > win ? p.stream_elems - win : 1);
         size_t idx = lane;
         float acc = 0.0f;

@@ -101,6 +101,17 @@ def test_mixes_run_clean(weights, gplk, cuda):
     torch.cuda.synchronize()
 
 
+def test_small_stream_buffer_stays_in_bounds(gplk, cuda):
+    """The smallest accepted streaming buffer (64 KiB) is smaller than the L2
+    role's 4 MiB window; the window is clamped to the buffer."""
+    import torch
+
+    cfg, *_rest = _setup(gplk, cuda, [0, 0, 1, 0, 0, 0, 1, 0], inner=64, verify=False, stream_mib=1)
+    cfg.stream_bytes = 64 << 10
+    gplk.powervirus_launch(cfg)
+    torch.cuda.synchronize()
+
+
 def test_ramp_block_counts(gplk, cuda):
     import torch
 
