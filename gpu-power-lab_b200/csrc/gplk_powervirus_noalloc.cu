@@ -1,0 +1,120 @@
+// gplk_powervirus_noalloc.cu - the powervirus launch for callers that cannot
+// allocate device memory.
+//
+// gplk_powervirus_launch works on two buffers whose contents nobody reads:
+// the streaming buffer behind the DRAM and L2 roles, and the atomic sink.
+// Its caller has to cudaMalloc them. Some callers cannot:
+//   - a load generator injected into another application's process, where
+//     that application's allocator (a framework's caching allocator, an MPS
+//     client limit) owns and budgets the device memory, so an extra
+//     cudaMalloc fails or takes memory the application counts on;
+//   - a duty-cycled burst loop, where cudaMalloc/cudaFree may synchronise the
+//     device and would cut an idle gap into the power wave being measured.
+// This entry point keeps both buffers in one file-scope device array instead,
+// sized for at most GPLK_PV_NOALLOC_MAX_STREAM_BYTES of streaming window plus
+// the sink. Every GPU that loads libgplk holds the array until the process
+// exits.
+//
+// Set-up: the first call on each device, with that device current, looks up
+// the array's device address with cudaGetSymbolAddress (the array's name in
+// host code is only a host-side stand-in, never a device address) and fills
+// the streaming window with a byte pattern, then synchronises the caller's
+// stream once. Make that first call before any stream capture.
+// Every call clears the sink before launching, because the atomics of the
+// previous call leave their counts in it. All calls share the array: calls
+// that overlap on the GPU (other streams, other threads) race on the sink.
+#include <cstdio>
+#include <mutex>
+
+#include "gplk_ptx.cuh"
+
+namespace gplk {
+namespace pv_noalloc {
+
+constexpr size_t kSinkBytes = 8192;  // 1 + 1024 floats, rounded up to 256-byte granules
+constexpr size_t kMaxStreamBytes = GPLK_PV_NOALLOC_MAX_STREAM_BYTES;
+constexpr size_t kScratchBytes = kSinkBytes + kMaxStreamBytes;
+constexpr unsigned char kStreamPattern = 0x3c;
+
+static __device__ __align__(256) unsigned char g_pv_scratch[kScratchBytes];
+
+struct DeviceScratch {
+    unsigned char* base = nullptr;  // device address of g_pv_scratch on this device
+    bool ready = false;
+};
+
+static DeviceScratch g_dev_scratch[64];
+static std::mutex g_dev_scratch_mu;
+
+// Once per device, with the device current: resolve the device address and
+// fill the streaming window.
+static int device_scratch(int dev, cudaStream_t stream, unsigned char** base) {
+    std::lock_guard<std::mutex> lock(g_dev_scratch_mu);
+    DeviceScratch& s = g_dev_scratch[dev];
+    if (!s.ready) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_pv_scratch) != cudaSuccess || p == nullptr)
+            return GPLK_STATUS_CUDA_ERROR;
+        unsigned char* b = static_cast<unsigned char*>(p);
+        if (cudaMemsetAsync(b + kSinkBytes, kStreamPattern, kMaxStreamBytes, stream) != cudaSuccess ||
+            cudaStreamSynchronize(stream) != cudaSuccess)
+            return GPLK_STATUS_CUDA_ERROR;
+        s.base = b;
+        s.ready = true;
+    }
+    *base = s.base;
+    return GPLK_STATUS_OK;
+}
+
+}  // namespace pv_noalloc
+}  // namespace gplk
+
+extern "C" int gplk_powervirus_launch_noalloc(const unsigned char* role_map, size_t stream_bytes, int blocks,
+                                              int inner, float* verify_out, const uint8_t* mma_a,
+                                              const uint8_t* mma_b, float* mma_out, cudaStream_t stream) {
+    using namespace gplk;
+    namespace nz = gplk::pv_noalloc;
+    if (!role_map || inner <= 0 || blocks < 0) return GPLK_STATUS_BAD_ARG;
+    if (stream_bytes > nz::kMaxStreamBytes) {
+        fprintf(stderr,
+                "gplk_powervirus_launch_noalloc: stream_bytes %zu exceeds the static scratch maximum of "
+                "%zu bytes (GPLK_PV_NOALLOC_MAX_STREAM_BYTES); use gplk_powervirus_launch with a caller "
+                "buffer for larger windows\n",
+                stream_bytes, (size_t)nz::kMaxStreamBytes);
+        return GPLK_STATUS_BAD_ARG;
+    }
+    if (stream_bytes < (64u << 10) || (stream_bytes & 15u)) return GPLK_STATUS_BAD_ARG;
+    if ((mma_a && !aligned16(mma_a)) || (mma_b && !aligned16(mma_b))) return GPLK_STATUS_BAD_ARG;
+    DeviceInfo d;
+    int st = require_sm100(&d);
+    if (st != GPLK_STATUS_OK) return st;
+    const int smem = (int)sizeof(pv::Smem) + 1024;
+    if (smem > d.max_smem_optin) return GPLK_STATUS_UNSUPPORTED;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return GPLK_STATUS_CUDA_ERROR;
+    unsigned char* base = nullptr;
+    st = nz::device_scratch(dev, stream, &base);
+    if (st != GPLK_STATUS_OK) return st;
+    static thread_local uint64_t configured = 0;
+    if (!(configured & (1ull << dev))) {
+        if (cudaFuncSetAttribute(pv::pv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+            return GPLK_STATUS_LAUNCH_FAIL;
+        configured |= 1ull << dev;
+    }
+    // The sink starts every call at zero, as a freshly cleared caller sink would.
+    if (cudaMemsetAsync(base, 0, nz::kSinkBytes, stream) != cudaSuccess) return GPLK_STATUS_CUDA_ERROR;
+    pv::Params p;
+    p.role_map = role_map;
+    p.stream_buf = reinterpret_cast<const float4*>(base + nz::kSinkBytes);
+    p.stream_elems = stream_bytes / sizeof(float4);
+    p.stream_chunks = stream_bytes / pv::kChunk;
+    p.sink = reinterpret_cast<float*>(base);
+    p.verify_out = reinterpret_cast<uint32_t*>(verify_out);
+    p.mma_a = mma_a;
+    p.mma_b = mma_b;
+    p.mma_out = mma_out;
+    p.inner = inner;
+    const int grid = blocks > 0 ? blocks : d.sm_count;
+    pv::pv_kernel<<<grid, pv::kThreads, smem, stream>>>(p);
+    return launch_status(cudaGetLastError());
+}

@@ -5,3 +5,4 @@
 #include "gplk_sgemm.cu"
 #include "gplk_gemm_tc.cu"
 #include "gplk_powervirus.cu"
+#include "gplk_powervirus_noalloc.cu"

@@ -95,6 +95,9 @@ def lib() -> ctypes.CDLL:
         L.gplk_pv_build_role_map.restype = None
         L.gplk_pv_build_role_map.argtypes = [_p, _p, _p]
         L.gplk_pv_block_threads.restype = _i
+    if hasattr(L, "gplk_powervirus_launch_noalloc"):
+        L.gplk_powervirus_launch_noalloc.restype = _i
+        L.gplk_powervirus_launch_noalloc.argtypes = [_p, _sz, _i, _i, _p, _p, _p, _p, _p]
     _lib = L
     return L
 
@@ -188,3 +191,23 @@ def pv_block_threads() -> int:
 
 def powervirus_launch(cfg: PvCfg, stream=None) -> None:
     _check("gplk_powervirus_launch", lib().gplk_powervirus_launch(ctypes.byref(cfg), _stream(stream)))
+
+
+PV_NOALLOC_MAX_STREAM_BYTES = 32 << 20
+
+
+def powervirus_launch_noalloc(role_map, stream_bytes: int, inner: int, blocks: int = 0, verify_out=None,
+                              mma=None, stream=None) -> None:
+    """The powervirus launch that allocates nothing (gplk_powervirus_launch_noalloc):
+    for callers that cannot cudaMalloc, such as a load generator running inside
+    another application's process whose allocator owns the device memory.
+    The streaming window and the atomic sink live in a static array inside
+    libgplk (window at most PV_NOALLOC_MAX_STREAM_BYTES). role_map: uint8 CUDA
+    tensor of 64 slots; mma: optional (a, b, out) tensors as for PvCfg."""
+    a = b = out = None
+    if mma is not None:
+        a, b, out = mma
+    ptr = lambda t: t.data_ptr() if t is not None else None
+    _check("gplk_powervirus_launch_noalloc",
+           lib().gplk_powervirus_launch_noalloc(ptr(role_map), stream_bytes, blocks, inner, ptr(verify_out),
+                                                ptr(a), ptr(b), ptr(out), _stream(stream)))

@@ -154,6 +154,34 @@ void gplk_pv_build_role_map(const int weights[GPLK_PV_ROLE_COUNT], unsigned char
 /* Threads per powervirus block (warps = value / 32). */
 int gplk_pv_block_threads(void);
 
+/* ------------------------------------------------------------ powervirus, no caller allocation
+ * This entry point has no counterpart in the reference.
+ *
+ * The same kernel as gplk_powervirus_launch, for callers that cannot call
+ * cudaMalloc: a load generator running inside another application's process
+ * whose allocator owns the device memory, or a duty-cycled burst loop where
+ * an allocation could synchronise the device mid-burst. The streaming
+ * window (read by the DRAM and L2 roles) and the atomic sink live in one
+ * static device array inside libgplk, held by every GPU that loads the
+ * library until the process exits.
+ *
+ * The caller passes the inputs (role_map; optional mma_a/mma_b tiles) and the
+ * outputs (optional verify_out, mma_out), as for gplk_powervirus_launch.
+ * stream_bytes picks the window size: a multiple of 16 in
+ * [64 KiB, GPLK_PV_NOALLOC_MAX_STREAM_BYTES]; a larger size is rejected with
+ * GPLK_STATUS_BAD_ARG and a message on stderr. A 32 MiB window fits in L2,
+ * so in this variant the DRAM role streams mostly from L2, not HBM.
+ *
+ * The first call on a device (with that device current) resolves the
+ * array's address, fills the window with the byte 0x3c and synchronises
+ * `stream`; make it before any stream capture. Each call zeroes the sink.
+ * All calls share the array, so calls that overlap on the GPU race on it.
+ * Allocates nothing: no cudaMalloc, cudaFree or allocating library call. */
+#define GPLK_PV_NOALLOC_MAX_STREAM_BYTES ((size_t)32 << 20)
+int gplk_powervirus_launch_noalloc(const unsigned char *role_map, size_t stream_bytes, int blocks,
+                                   int inner, float *verify_out, const uint8_t *mma_a,
+                                   const uint8_t *mma_b, float *mma_out, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
