@@ -39,7 +39,7 @@ TRIAD_BYTES = 12 * TRIAD_N  # read b, read c, write a (runner/src/workload_util.
 # dram__bytes_read.sum + dram__bytes_write.sum per launch from ncu captures
 # (profiles/*.md, scaled to the full launch where the capture was smaller).
 NCU_TRAFFIC = {
-    "memstream": None,
+    "memstream": 12.59e9,  # profiles/memstream_triad_2p30.md: 8 x 1.574 GB (3 x 2^27 capture)
     "sgemm": None,
     "fp8": None,
     "nvfp4": None,

@@ -6,3 +6,4 @@
 #include "gplk_gemm_tc.cu"
 #include "gplk_powervirus.cu"
 #include "gplk_powervirus_noalloc.cu"
+#include "gplk_gemm_lt.cu"

@@ -1,0 +1,130 @@
+"""The drop-in load generators inside the reference's own runner host.
+
+oracle/runner_build.sh links the reference's kept host (CLI, NVML sampler,
+summary emitter, probe, fft/observe/nccl rungs) with this repository's
+drop-in workload drivers and libgplk (oracle/_ref/gpu-power-runner-gplk),
+and builds the unmodified reference runner beside it
+(oracle/_ref/gpu-power-runner). These tests run rungs end to end through
+the runner's CLI contract and read its summary JSON and NDJSON telemetry.
+No power-limit or clock flag is ever passed: the runners leave the GPU's
+settings alone.
+"""
+from __future__ import annotations
+
+import json
+import os
+import subprocess
+from pathlib import Path
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+REPO = Path(__file__).resolve().parent.parent
+GPLK_RUNNER = REPO / "oracle/_ref/gpu-power-runner-gplk"
+REF_RUNNER = REPO / "oracle/_ref/gpu-power-runner"
+
+needs_runner = pytest.mark.skipif(not GPLK_RUNNER.exists(), reason="runner not built (oracle/runner_build.sh)")
+
+
+def run_rung(binary: Path, tmp_path: Path, *args: str, env: dict | None = None, timeout: int = 300):
+    summary = tmp_path / "summary.json"
+    metrics = tmp_path / "metrics.ndjson"
+    cmd = [str(binary), "--warmup-sec", "1", "--steady-sec", "2", "--sample-hz", "50",
+           "--out-summary", str(summary), "--out-metrics", str(metrics), *args]
+    e = dict(os.environ)
+    e.update(env or {})
+    res = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout, env=e)
+    s = json.loads(summary.read_text()) if summary.exists() else None
+    lines = metrics.read_text().splitlines() if metrics.exists() else []
+    return res, s, lines
+
+
+def _ok(res, s):
+    assert res.returncode == 0, res.stderr[-2000:]
+    assert s is not None and s["result"] == "ok", (s or {}).get("error_message")
+
+
+@needs_runner
+def test_memstream_rung(tmp_path):
+    res, s, lines = run_rung(GPLK_RUNNER, tmp_path, "--op", "memstream", "--size", "32768",
+                             env={"GPL_TRIAD_SCALAR": "3.0"})
+    _ok(res, s)
+    assert s["invocation"]["op"] == "memstream"
+    assert s["throughput"]["op_specific_unit"] == "GB/s"
+    assert s["throughput"]["value"] > 5000.0
+    assert s["compute"]["iterations"] > 100
+    phases = {json.loads(l).get("phase") for l in lines}
+    assert "steady" in phases or 2 in phases or "STEADY" in phases
+
+
+@needs_runner
+@pytest.mark.parametrize("prec,size,min_tflops", [("fp32", 1024, 10.0), ("fp8", 8192, 1000.0),
+                                                  ("fp4", 8192, 1000.0), ("bf16", 8192, 500.0)])
+def test_gemm_ladder_rungs(prec, size, min_tflops, tmp_path):
+    res, s, _ = run_rung(GPLK_RUNNER, tmp_path, "--op", "sgemm", "--precision", prec, "--size", str(size))
+    _ok(res, s)
+    assert s["compute"]["tflops_measured"] > min_tflops, s["compute"]
+
+
+@needs_runner
+@pytest.mark.skipif(not REF_RUNNER.exists(), reason="reference runner not built")
+def test_reference_runner_rejects_fp4_on_sgemm(tmp_path):
+    """The reference cannot run the NVFP4 rung at all (runner/src/workload_gemm.c:84-89
+    rejects fp8/fp4 on this op); the drop-in runs it (test above)."""
+    res, s, _ = run_rung(REF_RUNNER, tmp_path, "--op", "sgemm", "--precision", "fp4", "--size", "4096")
+    assert res.returncode == 5
+    assert s is not None and s["result"] == "cuda_error"
+
+
+@needs_runner
+def test_powervirus_default_mix(tmp_path):
+    res, s, lines = run_rung(GPLK_RUNNER, tmp_path, "--op", "powervirus", "--size", "8192")
+    _ok(res, s)
+    assert s["compute"]["iterations"] > 0
+    assert s["power"]["avg_w"] > 0 and s["power"]["pct_of_enforced_limit"] > 0
+    assert len(lines) > 10
+
+
+@needs_runner
+@pytest.mark.parametrize("prec", ["fp8", "fp4"])
+def test_powervirus_tensor_stream_narrow_formats(prec, tmp_path):
+    """--tensor-backend cublas with fp8/fp4: GEMMs on a concurrent stream through
+    the drop-in gpl_lt_* (libgplk tcgen05). Tensor-only, so FLOPs are counted."""
+    res, s, _ = run_rung(GPLK_RUNNER, tmp_path, "--op", "powervirus", "--tensor-backend", "cublas",
+                         "--precision", prec, "--size", "8192", "--mix-fma", "0", "--mix-dram", "0")
+    _ok(res, s)
+    assert s["compute"]["tflops_measured"] > 1000.0
+
+
+@needs_runner
+def test_powervirus_duty_cycle_and_ramp(tmp_path):
+    res, s, _ = run_rung(GPLK_RUNNER, tmp_path, "--op", "powervirus", "--size", "4096", "--duty-on-ms", "100",
+                         "--duty-off-ms", "100", "--duty-ramp", "linear")
+    _ok(res, s)
+    assert s["transient"]["duty_on_ms"] == 100.0
+
+
+@needs_runner
+def test_powervirus_fixed_work(tmp_path):
+    res, s, _ = run_rung(GPLK_RUNNER, tmp_path, "--op", "powervirus", "--size", "1024", "--iters", "64",
+                         "--mix-tensor", "1", "--mix-fma", "2", "--mix-dram", "1", "--mix-sfu", "1",
+                         "--mix-int32", "1", "--mix-smem", "1", "--mix-l2", "1", "--mix-atomic", "1")
+    _ok(res, s)
+    assert s["compute"]["iterations"] >= 64
+    assert s["efficiency"]["mode"] == "fixed_work"
+
+
+@needs_runner
+@pytest.mark.skipif(not REF_RUNNER.exists(), reason="reference runner not built")
+def test_memstream_beats_reference_runner(tmp_path):
+    """Same rung, same flags, same box: the drop-in's GB/s against the
+    reference runner's stream_triad_kernel."""
+    (tmp_path / "a").mkdir()
+    (tmp_path / "b").mkdir()
+    res_r, s_r, _ = run_rung(REF_RUNNER, tmp_path / "a", "--op", "memstream", "--size", "32768")
+    _ok(res_r, s_r)
+    res_g, s_g, _ = run_rung(GPLK_RUNNER, tmp_path / "b", "--op", "memstream", "--size", "32768")
+    _ok(res_g, s_g)
+    print(f"memstream GB/s: reference {s_r['throughput']['value']:.0f}, drop-in {s_g['throughput']['value']:.0f}")
+    assert s_g["throughput"]["value"] > s_r["throughput"]["value"]
