@@ -74,6 +74,7 @@ struct Params {
     int m_tiles, n_tiles, k_stages;
     int sf_kblocks4;       // NVFP4: ceil(K / 64) = 512-byte blocks per 128 rows
     int sf_row_blocks_b;   // NVFP4: ceil(N / 128) row blocks in SFB
+    int tma_store;         // pair kernel: write D with TMA stores (M % 8 == 0)
 };
 
 __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int& mt, int& nt,
@@ -341,8 +342,12 @@ constexpr int kPairHalf = 128 * BK_BYTES;          // 16 KiB: 128 rows x 128 B
 constexpr int kPairStageBytes = 2 * kPairHalf;     // A half + B half
 constexpr int kPairGroupM = 16;
 
+constexpr int kOutChunkCols = 32;                   // columns of D per TMA store
+constexpr int kOutChunkBytes = 128 * kOutChunkCols * 2;  // 128 rows x 32 BF16 = 8 KiB
+
 struct __align__(1024) PairSmem {
     uint8_t stage[kPairStages][kPairStageBytes];
+    uint8_t out_stage[2][kOutChunkBytes];  // epilogue staging for TMA stores of D
     uint64_t full[kPairStages];
     uint64_t empty[kPairStages];
     uint64_t acc_full[2];
@@ -350,11 +355,12 @@ struct __align__(1024) PairSmem {
     uint64_t drain;
     uint32_t tmem_base;
     int abort;
+    int epi_fail;
 };
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_pair_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                         const Params p) {
+                         const __grid_constant__ CUtensorMap tmD, const Params p) {
     constexpr int S = kPairStages;
     extern __shared__ uint8_t smem_raw[];
     PairSmem& sm = *reinterpret_cast<PairSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -377,11 +383,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         mbar_init(&sm.drain, 1);
         sm.abort = 0;
+        sm.epi_fail = 0;
         fence_barrier_init();
     }
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
+        if (p.tma_store) tma_prefetch_desc(&tmD);
     }
     if (warp == 1) {
         tmem_alloc_pair(&sm.tmem_base, 512);
@@ -476,27 +484,60 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             mbar_wait_cluster(&sm.drain, 0, &dummy, 0x0413, 100000000ull);
         }
     } else {
+        // Epilogue: warps 2..5 read TMEM lanes 32*(warp%4).. (= rows of this
+        // CTA's half). With TMA stores, each 32-column chunk is staged as
+        // [column][row] BF16 in shared memory (double-buffered) and written
+        // by one bulk tensor store; the TMA unit clips partial tiles.
         const uint32_t quarter = warp & 3u;
         const int row_in_half = (int)(quarter * 32 + lane);
         const float scale = __ldg(p.scale_a) * __ldg(p.scale_b);
+        const bool issuer = warp == 2 && lane == 0;
         int acc = 0;
         uint32_t acc_phase = 0;
+        uint32_t chunk_seq = 0;
         for (int t = cluster; t < num_tiles; t += nclusters) {
             int mt, nt;
             tile_coords(t, p.m_tiles, p.n_tiles, mt, nt, kPairGroupM);
-            if (!mbar_wait_cluster(&sm.acc_full[acc], acc_phase, &sm.abort, 0x0421)) break;
+            // All four epilogue warps leave together if any of them gave up.
+            if (!mbar_wait_sleepy(&sm.acc_full[acc], acc_phase, &sm.abort, 0x0421, true)) sm.epi_fail = 1;
+            named_sync(1, 128);
+            if (*(volatile int*)&sm.epi_fail) break;
             tc_fence_after();
-            const int m = mt * 256 + (int)rank * 128 + row_in_half;
+            const int m0 = mt * 256 + (int)rank * 128;
+            const int m = m0 + row_in_half;
             const int n_base = nt * 256;
             const uint32_t t_addr = tmem + ((quarter * 32u) << 16) + (uint32_t)acc * 256u;
-            uint16_t* drow = p.D + m;
-            const size_t ldd = (size_t)p.M;
+            const uint32_t acc_empty_leader = mapa_shared(smem_u32(&sm.acc_empty[acc]), 0);
 #pragma unroll 1
             for (int c = 0; c < 8; ++c) {
                 uint32_t r[32];
                 tmem_ld_32x32b_x32(t_addr + 32u * c, r);
                 tmem_ld_wait();
-                if (m < p.M) {
+                if (c == 7) {  // the accumulator is in registers: release it to the MMA
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(acc_empty_leader);
+                }
+                if (p.tma_store) {
+                    uint16_t* stg = reinterpret_cast<uint16_t*>(sm.out_stage[chunk_seq & 1u]);
+                    if (issuer) bulk_wait_read<1>();  // the store that last used this buffer has read it
+                    named_sync(1, 128);
+#pragma unroll
+                    for (int j = 0; j < 32; j += 2) {
+                        const uint32_t v = pack_bf16x2(__uint_as_float(r[j]) * scale, __uint_as_float(r[j + 1]) * scale);
+                        stg[j * 128 + row_in_half] = (uint16_t)(v & 0xFFFFu);
+                        stg[(j + 1) * 128 + row_in_half] = (uint16_t)(v >> 16);
+                    }
+                    fence_proxy_async_smem();
+                    named_sync(1, 128);
+                    if (issuer && m0 < p.M && n_base + kOutChunkCols * c < p.N) {  // skip boxes wholly outside D
+                        tma_store_2d(&tmD, stg, m0, n_base + kOutChunkCols * c);
+                        bulk_commit();
+                    }
+                    ++chunk_seq;
+                } else if (m < p.M) {
+                    uint16_t* drow = p.D + m;
+                    const size_t ldd = (size_t)p.M;
 #pragma unroll
                     for (int j = 0; j < 32; j += 2) {
                         const uint32_t v = pack_bf16x2(__uint_as_float(r[j]) * scale, __uint_as_float(r[j + 1]) * scale);
@@ -506,14 +547,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     }
                 }
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&sm.acc_empty[acc]), 0));
             if (++acc == 2) {
                 acc = 0;
                 acc_phase ^= 1u;
             }
         }
+        if (issuer) bulk_wait<0>();  // every store of D has completed
     }
 
     tc_fence_before();
@@ -636,10 +675,17 @@ static int launch_pair_fp8(const uint8_t* A, const uint8_t* B, uint16_t* D, int 
     p.m_tiles = (M + 255) / 256;
     p.n_tiles = (N + 255) / 256;
     p.k_stages = (K + BK_BYTES - 1) / BK_BYTES;
+    CUtensorMap tmD;
+    memset(&tmD, 0, sizeof(tmD));
+    p.tma_store = (M % 8 == 0) && aligned16(D);
+    if (p.tma_store) {
+        st = encode_tmap_2d_u16(&tmD, D, (uint64_t)M, (uint64_t)N, (uint64_t)M * 2, 128, kOutChunkCols);
+        if (st != GPLK_STATUS_OK) return st;
+    }
     const int tiles = p.m_tiles * p.n_tiles;
     int clusters = pair_cluster_capacity(d, smem);
     if (clusters > tiles) clusters = tiles;
-    gemm_pair_fp8_kernel<<<2 * clusters, kThreads, smem, stream>>>(tmA, tmB, p);
+    gemm_pair_fp8_kernel<<<2 * clusters, kThreads, smem, stream>>>(tmA, tmB, tmD, p);
     return launch_status(cudaGetLastError());
 }
 

@@ -286,6 +286,57 @@ __host__ __device__ constexpr uint32_t idesc_nvf4(int M, int N) {
            | ((uint32_t)(M >> 4) << 24);   // M / 16
 }
 
+// Bounded wait for waits that are expected to be long and are not on the
+// critical path (an epilogue waiting for a whole main loop): backs off with
+// nanosleep so the waiting warp leaves issue slots to the TMA and MMA warps.
+__device__ __forceinline__ bool mbar_wait_sleepy(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                 int site, bool cluster_scope,
+                                                 uint64_t budget_ns = kWaitBudgetNs) {
+    auto probe = [&]() {
+        if (cluster_scope) {
+            uint32_t ok;
+            asm volatile(
+                "{\n\t.reg .pred p;\n\t"
+                "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+                "selp.u32 %0, 1, 0, p;\n\t}"
+                : "=r"(ok)
+                : "r"(smem_u32(bar)), "r"(parity)
+                : "memory");
+            return ok != 0;
+        }
+        return mbar_try_wait(bar, parity);
+    };
+    if (probe()) return true;
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t spins = 0;
+    while (true) {
+        __nanosleep(256);
+        if (probe()) return true;
+        if ((++spins & 15u) == 0) {
+            if (*abort_flag) return false;
+            if (globaltimer_ns() - t0 > budget_ns) {
+                record_error(GPLK_STATUS_DEVICE_TIMEOUT, site);
+                *abort_flag = 1;
+                return false;
+            }
+        }
+    }
+}
+
+// 2-D tiled TMA store from this CTA's shared memory (bulk-group tracked).
+// Elements of the box outside the tensor are not written.
+__device__ __forceinline__ void tma_store_2d(const void* tmap, const void* src, int32_t c0, int32_t c1) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(tmap)),
+                 "r"(smem_u32(src)), "r"(c0), "r"(c1)
+                 : "memory");
+}
+
+// Named barrier among `nthreads` threads (a multiple of 32) with id `id`.
+__device__ __forceinline__ void named_sync(uint32_t id, uint32_t nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // ---------------------------------------------------------------- CTA pairs (cta_group::2)
 // A pair is a 2-CTA cluster whose rank-0 CTA (the leader) issues MMAs that
 // read operands from both CTAs' shared memory and write both CTAs' TMEM.

@@ -18,6 +18,7 @@ from __future__ import annotations
 import ctypes
 import json
 import sys
+import time
 from pathlib import Path
 
 REPO = Path(__file__).resolve().parent.parent
@@ -27,6 +28,72 @@ import torch  # noqa: E402
 
 import gplk  # noqa: E402
 import oracle  # noqa: E402
+
+
+class Sampler:
+    """NVML SM clock and power every 20 ms while a case runs."""
+
+    def __init__(self):
+        import threading
+
+        import pynvml
+
+        pynvml.nvmlInit()
+        self.nv = pynvml
+        self.h = pynvml.nvmlDeviceGetHandleByIndex(torch.cuda.current_device())
+        self.samples = []
+        self.stop_ev = threading.Event()
+        self.thr = threading.Thread(target=self.run, daemon=True)
+
+    def run(self):
+        while not self.stop_ev.is_set():
+            self.samples.append((self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM),
+                                 self.nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0))
+            self.stop_ev.wait(0.02)
+
+    def __enter__(self):
+        self.thr.start()
+        return self
+
+    def __exit__(self, *exc):
+        self.stop_ev.set()
+        self.thr.join()
+
+    def median(self):
+        if not self.samples:
+            return None, None
+        c = sorted(x[0] for x in self.samples)
+        p = sorted(x[1] for x in self.samples)
+        return c[len(c) // 2], round(p[len(p) // 2], 1)
+
+
+def sustained(fn, seconds=1.0, warm_s=0.3):
+    """Time fn over about `seconds` after `warm_s` of warm-up; returns
+    (ms per call, median SM MHz, median W) for the timed window."""
+    s = torch.cuda.current_stream()
+    t0 = time.perf_counter()
+    calls = 0
+    while time.perf_counter() - t0 < warm_s or calls < 3:
+        fn()
+        calls += 1
+        if calls % 16 == 0:
+            torch.cuda.synchronize()
+    torch.cuda.synchronize()
+    per = max(1, int(calls / max(time.perf_counter() - t0, 1e-3) * 0.05))  # ~50 ms batches
+    with Sampler() as smp:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        n = 0
+        t1 = time.perf_counter()
+        while time.perf_counter() - t1 < seconds:
+            for _ in range(per):
+                fn()
+            n += per
+            torch.cuda.synchronize()
+        e1.record(s)
+        torch.cuda.synchronize()
+    mhz, watts = smp.median()
+    return e0.elapsed_time(e1) / n, mhz, watts
 
 
 def timed(fn, reps, warm=3):
@@ -52,11 +119,11 @@ def memstream(out):
     st = torch.cuda.current_stream().cuda_stream
     gb = lambda ms: 12 * n / (ms / 1e3) / 1e9
     out["memstream_GBps"] = {
-        "reference_stream_triad_kernel": gb(timed(lambda: L.ref_triad_launch(a.data_ptr(), b.data_ptr(), c.data_ptr(), 3.0, n, st), 100)),
-        "gplk_triad_vec4": gb(timed(lambda: gplk.triad(a, b, c, 3.0), 100)),
-        "gplk_triad_bulk": gb(timed(lambda: gplk.triad(a, b, c, 3.0, bulk=True), 100)),
-        "gplk_copy": 8 * n / (timed(lambda: gplk.copy(a, b), 100) / 1e3) / 1e9,
-        "torch_copy": 8 * n / (timed(lambda: a.copy_(b), 100) / 1e3) / 1e9,
+        "reference_stream_triad_kernel": gb(sustained(lambda: L.ref_triad_launch(a.data_ptr(), b.data_ptr(), c.data_ptr(), 3.0, n, st))[0]),
+        "gplk_triad_vec4": gb(sustained(lambda: gplk.triad(a, b, c, 3.0))[0]),
+        "gplk_triad_bulk": gb(sustained(lambda: gplk.triad(a, b, c, 3.0, bulk=True))[0]),
+        "gplk_copy": 8 * n / (sustained(lambda: gplk.copy(a, b))[0] / 1e3) / 1e9,
+        "torch_copy": 8 * n / (sustained(lambda: a.copy_(b))[0] / 1e3) / 1e9,
     }
     del a, b, c
 
@@ -69,8 +136,8 @@ def sgemm(out):
     C = torch.empty(n, n, device="cuda")
     tf = lambda ms: 2 * n ** 3 / (ms / 1e3) / 1e12
     out["sgemm_1024_TFLOPs"] = {
-        "cublas_fp32": tf(timed(lambda: torch.matmul(A, B, out=C), 200)),
-        "gplk_sgemm": tf(timed(lambda: gplk.sgemm(A, B, C), 200)),
+        "cublas_fp32": tf(sustained(lambda: torch.matmul(A, B, out=C))[0]),
+        "gplk_sgemm": tf(sustained(lambda: gplk.sgemm(A, B, C))[0]),
     }
 
 
@@ -106,16 +173,20 @@ def fp8(out):
         assert cudart.cudaMemcpy(ptrs[0], A.data_ptr(), n * n, 3) == 0
         assert cudart.cudaMemcpy(ptrs[1], B.data_ptr(), n * n, 3) == 0
         torch.cuda.synchronize()
-        res[label] = {
-            "reference_gemm_lt_cublaslt": tf(timed(lambda: L.gpl_lt_enqueue(g, 1), 100)),
-            "gplk_gemm_fp8_tn": tf(timed(lambda: gplk.gemm_fp8_tn(A, B, D, s, s), 100)),
-        }
+        r = {}
+        for name, fn in (("reference_gemm_lt_cublaslt", lambda: L.gpl_lt_enqueue(g, 1)),
+                         ("gplk_gemm_fp8_tn", lambda: gplk.gemm_fp8_tn(A, B, D, s, s)),
+                         ("reference_gemm_lt_cublaslt_again", lambda: L.gpl_lt_enqueue(g, 1))):
+            ms, mhz, w = sustained(fn)
+            r[name] = {"tflops": round(tf(ms), 1), "sm_mhz": mhz, "watts": w}
+        res[label] = r
     out["fp8_8192_TFLOPs"] = res
     L.gpl_lt_free(g)
     L.ref_lt_delete(g)
 
 
 def nvfp4(out):
+    """Identical random packed operands and 0x38 (1.0) block scales for both."""
     res = {}
     for n in (2048, 4096, 8192, 16384):
         A = torch.randint(0, 256, (n, n // 2), dtype=torch.uint8, device="cuda")
@@ -125,15 +196,19 @@ def nvfp4(out):
         D = torch.empty(n, n, dtype=torch.bfloat16, device="cuda")
         al = torch.ones(1, device="cuda")
         ws = torch.empty(32 << 20, dtype=torch.uint8, device="cuda")
-        reps = max(5, int(2e13 / (2 * n ** 3)))
-        ms = ctypes.c_float(0)
-        rc = oracle.lt_lib().oracle_lt_gemm_nvfp4_tn_timed(A.data_ptr(), B.data_ptr(), SF.data_ptr(), SF.data_ptr(),
-                                                           D.data_ptr(), n, n, n, 1.0, ws.data_ptr(), ws.numel(), reps,
-                                                           torch.cuda.current_stream().cuda_stream, ctypes.byref(ms))
         tf = lambda m: 2 * n ** 3 / (m / 1e3) / 1e12
+        ms_ours, mhz_o, w_o = sustained(lambda: gplk.gemm_nvfp4_tn(A, B, SF, SF, D, n, al))
+        reps = max(5, int(1000.0 / ms_ours))  # about one second
+        ms = ctypes.c_float(0)
+        with Sampler() as smp:
+            rc = oracle.lt_lib().oracle_lt_gemm_nvfp4_tn_timed(
+                A.data_ptr(), B.data_ptr(), SF.data_ptr(), SF.data_ptr(), D.data_ptr(), n, n, n, 1.0,
+                ws.data_ptr(), ws.numel(), reps, torch.cuda.current_stream().cuda_stream, ctypes.byref(ms))
+        mhz_l, w_l = smp.median()
         res[n] = {
-            "cublaslt_nvfp4": tf(ms.value / reps) if rc == 0 else f"rc={rc}",
-            "gplk_gemm_nvfp4_tn": tf(timed(lambda: gplk.gemm_nvfp4_tn(A, B, SF, SF, D, n, al), reps)),
+            "cublaslt_nvfp4": {"tflops": round(tf(ms.value / reps), 1), "sm_mhz": mhz_l, "watts": w_l}
+            if rc == 0 else f"rc={rc}",
+            "gplk_gemm_nvfp4_tn": {"tflops": round(tf(ms_ours), 1), "sm_mhz": mhz_o, "watts": w_o},
         }
     out["nvfp4_TFLOPs"] = res
 

@@ -40,7 +40,7 @@ def _run(gplk, qa, sa, qb, sb, cuda):
     return D.float().cpu().numpy()
 
 
-@pytest.mark.parametrize("mnk", [(128, 256, 128), (256, 256, 256), (512, 512, 1024), (1024, 768, 512),
+@pytest.mark.parametrize("mnk", [(128, 256, 128), (256, 256, 256), (512, 512, 1024), (1024, 768, 512), (300, 520, 256), (136, 264, 384),
                                  (200, 300, 512), (129, 257, 144), (1, 1, 16), (640, 1280, 2048)])
 def test_fp8_full_vs_oracle(mnk, gplk, oracle, cuda):
     M, N, K = mnk
