@@ -55,6 +55,7 @@ struct Traits {
 template <bool NVF4>
 struct __align__(1024) Smem {
     uint8_t stage[Traits<NVF4>::kStages][Traits<NVF4>::kStageBytes];
+    uint8_t out_stage[NVF4 ? 128 * 32 * 2 : 16];  // NVFP4 epilogue staging: 128 rows x 32 BF16
     uint64_t full[Traits<NVF4>::kStages];
     uint64_t empty[Traits<NVF4>::kStages];
     uint64_t acc_full[2];
@@ -62,10 +63,12 @@ struct __align__(1024) Smem {
     uint64_t drain;
     uint32_t tmem_base;
     int abort;
+    int epi_fail;
 };
 
 struct Params {
     uint16_t* D;
+    int group_m;           // raster group along M (tiles)
     const uint8_t* sfa;  // NVFP4 only
     const uint8_t* sfb;
     const float* scale_a;  // FP8: per-tensor scales; NVFP4: scale_a = alpha
@@ -91,7 +94,7 @@ __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int
 template <bool NVF4>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const Params p) {
+                   const __grid_constant__ CUtensorMap tmD, const Params p) {
     using TR = Traits<NVF4>;
     constexpr int S = TR::kStages;
     extern __shared__ uint8_t smem_raw[];
@@ -113,6 +116,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_init(&sm.drain, 1);
         sm.abort = 0;
+        sm.epi_fail = 0;
         fence_barrier_init();
     }
     if (warp == 0 && lane == 0) {
@@ -137,7 +141,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
                 int mt, nt;
-                tile_coords(t, p.m_tiles, p.n_tiles, mt, nt);
+                tile_coords(t, p.m_tiles, p.n_tiles, mt, nt, p.group_m);
                 for (int kb = 0; kb < p.k_stages; ++kb) {
                     if (!mbar_wait(&sm.empty[stage], phase ^ 1u, &sm.abort, 0x0201)) {
                         ok = false;
@@ -258,8 +262,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t acc_phase = 0;
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
             int mt, nt;
-            tile_coords(t, p.m_tiles, p.n_tiles, mt, nt);
-            if (!mbar_wait(&sm.acc_full[acc], acc_phase, &sm.abort, 0x0221)) break;
+            tile_coords(t, p.m_tiles, p.n_tiles, mt, nt, p.group_m);
+            // All four epilogue warps leave together if any of them gave up
+            // (the staged store path synchronises them with a named barrier).
+            if (!mbar_wait_sleepy(&sm.acc_full[acc], acc_phase, &sm.abort, 0x0221, false)) sm.epi_fail = 1;
+            named_sync(1, 128);
+            if (*(volatile int*)&sm.epi_fail) break;
             tc_fence_after();
             const int m = mt * BM + row_in_tile;
             const int n_base = nt * BN;
@@ -282,7 +290,29 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&sm.acc_empty[acc]);
-                if (m < p.M) {
+                if (p.tma_store) {
+                    // One 8 KiB staging buffer ([column][row] BF16, 32 columns):
+                    // wait for the previous store to read it, fill, store.
+                    const bool issuer = warp == 2 && lane == 0;
+                    uint16_t* stg = reinterpret_cast<uint16_t*>(sm.out_stage);
+                    const int m0 = mt * BM;
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        if (issuer) bulk_wait_read<0>();
+                        named_sync(1, 128);
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            stg[(2 * j) * 128 + row_in_tile] = (uint16_t)(packed[c * 16 + j] & 0xFFFFu);
+                            stg[(2 * j + 1) * 128 + row_in_tile] = (uint16_t)(packed[c * 16 + j] >> 16);
+                        }
+                        fence_proxy_async_smem();
+                        named_sync(1, 128);
+                        if (issuer && n_base + 32 * c < p.N) {
+                            tma_store_2d(&tmD, stg, m0, n_base + 32 * c);
+                            bulk_commit();
+                        }
+                    }
+                } else if (m < p.M) {
 #pragma unroll
                     for (int j = 0; j < 128; ++j) {
                         const int n = n_base + 2 * j;
@@ -316,6 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 acc_phase ^= 1u;
             }
         }
+        if (NVF4 && p.tma_store && warp == 2 && lane == 0) bulk_wait<0>();
     }
 
     tc_fence_before();
@@ -595,6 +626,7 @@ static int launch(const uint8_t* A, const uint8_t* B, const uint8_t* SFA, const 
     if (st != GPLK_STATUS_OK) return st;
 
     Params p;
+    memset(&p, 0, sizeof(p));
     p.D = D;
     p.sfa = SFA;
     p.sfb = SFB;
@@ -608,9 +640,19 @@ static int launch(const uint8_t* A, const uint8_t* B, const uint8_t* SFA, const 
     p.k_stages = (int)((row_bytes + BK_BYTES - 1) / BK_BYTES);
     p.sf_kblocks4 = (K + 63) / 64;
     p.sf_row_blocks_b = (N + 127) / 128;
+    // A wide raster group keeps B's row blocks in L2 across more M tiles
+    // (B is re-read from DRAM once per group).
+    p.group_m = NVF4 ? 32 : kGroupM;
+    CUtensorMap tmD;
+    memset(&tmD, 0, sizeof(tmD));
+    p.tma_store = NVF4 && (M % 8 == 0) && aligned16(D);
+    if (p.tma_store) {
+        st = encode_tmap_2d_u16(&tmD, D, (uint64_t)M, (uint64_t)N, (uint64_t)M * 2, 128, 32);
+        if (st != GPLK_STATUS_OK) return st;
+    }
     const int tiles = p.m_tiles * p.n_tiles;
     const int grid = tiles < d.sm_count ? tiles : d.sm_count;
-    gemm_tc_kernel<NVF4><<<grid, kThreads, smem, stream>>>(tmA, tmB, p);
+    gemm_tc_kernel<NVF4><<<grid, kThreads, smem, stream>>>(tmA, tmB, tmD, p);
     return launch_status(cudaGetLastError());
 }
 
