@@ -65,6 +65,7 @@ struct Params {
     const uint8_t* mma_b;
     float* mma_out;
     int inner;
+    uint64_t budget_ns;  // 0: fixed work; else every role continues until this long after block start
 };
 
 // Byte offset of (row, k) in a K-major tile staged with the 128-byte swizzle
@@ -115,6 +116,11 @@ __global__ void __launch_bounds__(kThreads, 1) pv_kernel(const Params p) {
     const int role = sm.role_of[warp];
     const int rank = sm.role_rank[warp];
     const int inner = p.inner;
+    // Time-boxed mode: after its fixed `inner` work, every role keeps going in
+    // small rounds until the shared deadline, so all units stay busy for the
+    // whole launch instead of the fastest roles idling behind the slowest.
+    const uint64_t deadline = p.budget_ns ? globaltimer_ns() + p.budget_ns : 0;
+    auto more = [&]() -> bool { return deadline != 0 && globaltimer_ns() < deadline && !*(volatile int*)&sm.abort; };
     const uint32_t global_warp = blockIdx.x * kWarps + warp;
     uint32_t keep_bits = 0;
     float keep = 0.0f;
@@ -135,7 +141,12 @@ __global__ void __launch_bounds__(kThreads, 1) pv_kernel(const Params p) {
                 const uint32_t d = sm.tmem_base;
                 const uint32_t a0 = smem_u32(sm.mma_a), b0 = smem_u32(sm.mma_b);
                 const uint32_t idesc = idesc_e4m3_f32(128, 256);
-                for (int it = 0; it < inner; ++it) {
+                int tiles = inner;
+                for (int it = 0;; ++it) {
+                    if (it == tiles) {
+                        if (!more()) break;
+                        tiles += 16;
+                    }
 #pragma unroll
                     for (int j = 0; j < 4; ++j)
                         mma_f8f6f4(d, desc_kmajor_sw128(a0 + 32 * j), desc_kmajor_sw128(b0 + 32 * j), idesc,
@@ -153,11 +164,14 @@ __global__ void __launch_bounds__(kThreads, 1) pv_kernel(const Params p) {
         float x0 = 1.0001f + (float)lane, x1 = 1.0002f, x2 = 1.0003f, x3 = 1.0004f;
         float x4 = 1.0005f, x5 = 1.0006f, x6 = 1.0007f, x7 = 1.0008f;
         const float m = 0.9999f, c = 1e-7f;
-        for (int i = 0; i < inner * 16; ++i) {
-            x0 = __fmaf_rn(x0, m, c); x1 = __fmaf_rn(x1, m, c);
-            x2 = __fmaf_rn(x2, m, c); x3 = __fmaf_rn(x3, m, c);
-            x4 = __fmaf_rn(x4, m, c); x5 = __fmaf_rn(x5, m, c);
-            x6 = __fmaf_rn(x6, m, c); x7 = __fmaf_rn(x7, m, c);
+        for (int steps = inner * 16;; steps = 256) {
+            for (int i = 0; i < steps; ++i) {
+                x0 = __fmaf_rn(x0, m, c); x1 = __fmaf_rn(x1, m, c);
+                x2 = __fmaf_rn(x2, m, c); x3 = __fmaf_rn(x3, m, c);
+                x4 = __fmaf_rn(x4, m, c); x5 = __fmaf_rn(x5, m, c);
+                x6 = __fmaf_rn(x6, m, c); x7 = __fmaf_rn(x7, m, c);
+            }
+            if (!more()) break;
         }
         keep = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(x0, x1), x2), x3), x4), x5), x6), x7);
         keep_bits = __float_as_uint(keep);
@@ -167,11 +181,14 @@ __global__ void __launch_bounds__(kThreads, 1) pv_kernel(const Params p) {
         const size_t stride = 65537;
         size_t idx = ((size_t)global_warp * 2654435761u + lane) % p.stream_elems;
         float acc = 0.0f;
-        for (int i = 0; i < inner * 4; ++i) {
-            const float4 v = p.stream_buf[idx];
-            acc += v.x + v.y + v.z + v.w;
-            idx += stride;
-            if (idx >= p.stream_elems) idx -= p.stream_elems;
+        for (int loads = inner * 4;; loads = 64) {
+            for (int i = 0; i < loads; ++i) {
+                const float4 v = p.stream_buf[idx];
+                acc += v.x + v.y + v.z + v.w;
+                idx += stride;
+                if (idx >= p.stream_elems) idx -= p.stream_elems;
+            }
+            if (!more()) break;
         }
         keep = acc;
         keep_bits = __float_as_uint(acc);
@@ -187,7 +204,7 @@ __global__ void __launch_bounds__(kThreads, 1) pv_kernel(const Params p) {
             const char* src = reinterpret_cast<const char*>(p.stream_buf);
             long long j = 0;
             bool ok = true;
-            for (; j < chunks; ++j) {
+            for (long long limit = chunks; j < limit || (more() && (limit = j + 1)); ++j) {
                 const int st = mine[j % n_mine];
                 if (j >= n_mine) {
                     const uint32_t par = (uint32_t)(((j / n_mine) - 1) & 1);
@@ -214,30 +231,39 @@ __global__ void __launch_bounds__(kThreads, 1) pv_kernel(const Params p) {
         const size_t base = ((size_t)blockIdx.x * 977) % (p.stream_elems > win ? p.stream_elems - win : 1);
         size_t idx = lane;
         float acc = 0.0f;
-        for (int i = 0; i < inner * 4; ++i) {
-            const float4 v = p.stream_buf[base + (idx % win)];
-            acc += v.x + v.y + v.z + v.w;
-            idx += 129;
+        for (int loads = inner * 4;; loads = 64) {
+            for (int i = 0; i < loads; ++i) {
+                const float4 v = p.stream_buf[base + (idx % win)];
+                acc += v.x + v.y + v.z + v.w;
+                idx += 129;
+            }
+            if (!more()) break;
         }
         keep = acc;
         keep_bits = __float_as_uint(acc);
     } else if (role == GPLK_PV_ROLE_SFU) {
         float a0 = 0.7f + lane * 0.01f, a1 = 1.1f, a2 = 0.3f, a3 = 1.7f;
-        for (int i = 0; i < inner * 4; ++i) {
-            a0 = __sinf(a0) + 1.0f;
-            a1 = __expf(a1 * 0.5f) * 0.5f;
-            a2 = __logf(a2 + 2.0f);
-            a3 = __frsqrt_rn(a3 + 1.0f) + 1.0f;
+        for (int steps = inner * 4;; steps = 64) {
+            for (int i = 0; i < steps; ++i) {
+                a0 = __sinf(a0) + 1.0f;
+                a1 = __expf(a1 * 0.5f) * 0.5f;
+                a2 = __logf(a2 + 2.0f);
+                a3 = __frsqrt_rn(a3 + 1.0f) + 1.0f;
+            }
+            if (!more()) break;
         }
         keep = a0 + a1 + a2 + a3;
         keep_bits = __float_as_uint(keep);
     } else if (role == GPLK_PV_ROLE_INT32) {
         uint32_t i0 = 0x9E3779B9u + lane, i1 = 0x85EBCA6Bu, i2 = 0xC2B2AE35u, i3 = 0x27D4EB2Fu;
-        for (int i = 0; i < inner * 16; ++i) {
-            i0 = i0 * 1664525u + 1013904223u;
-            i1 = i1 * 22695477u + 1u;
-            i2 = i2 * 1103515245u + 12345u;
-            i3 = i3 * 214013u + 2531011u;
+        for (int steps = inner * 16;; steps = 256) {
+            for (int i = 0; i < steps; ++i) {
+                i0 = i0 * 1664525u + 1013904223u;
+                i1 = i1 * 22695477u + 1u;
+                i2 = i2 * 1103515245u + 12345u;
+                i3 = i3 * 214013u + 2531011u;
+            }
+            if (!more()) break;
         }
         keep_bits = i0 ^ i1 ^ i2 ^ i3;
         keep = (float)(keep_bits & 0xFFFFu);
@@ -247,17 +273,24 @@ __global__ void __launch_bounds__(kThreads, 1) pv_kernel(const Params p) {
         mine[lane + 32] = 2.0f;
         __syncwarp();
         float acc = 0.0f;
-        for (int i = 0; i < inner * 8; ++i) {
-            const int j = (lane + i) & 31;
-            acc = __fmaf_rn(mine[j], 1.000001f, acc);
-            mine[j + 32] = acc;
+        int i = 0;
+        for (int steps = inner * 8;; steps = 256) {
+            for (const int end = i + steps; i < end; ++i) {
+                const int j = (lane + i) & 31;
+                acc = __fmaf_rn(mine[j], 1.000001f, acc);
+                mine[j + 32] = acc;
+            }
+            if (!more()) break;
         }
         keep = acc;
         keep_bits = __float_as_uint(acc);
     } else {  // ATOMIC
         float acc = 0.0f;
         const int slot = (int)((global_warp * 32 + lane) & (kAtomicSlots - 1));
-        for (int i = 0; i < inner; ++i) acc += atomicAdd(&p.sink[1 + slot], 1.0f);
+        for (int ops = inner;; ops = 16) {
+            for (int i = 0; i < ops; ++i) acc += atomicAdd(&p.sink[1 + slot], 1.0f);
+            if (!more()) break;
+        }
         keep = acc * 1e-30f;
         keep_bits = __float_as_uint(keep);
     }
@@ -377,6 +410,7 @@ extern "C" int gplk_powervirus_launch(const gplk_pv_cfg* cfg, cudaStream_t strea
     p.mma_b = cfg->mma_b;
     p.mma_out = cfg->mma_out;
     p.inner = cfg->inner;
+    p.budget_ns = cfg->budget_ns;
     const int grid = cfg->blocks > 0 ? cfg->blocks : d.sm_count;
     pv::pv_kernel<<<grid, pv::kThreads, smem, stream>>>(p);
     return launch_status(cudaGetLastError());

@@ -114,6 +114,7 @@ extern "C" int gplk_powervirus_launch_noalloc(const unsigned char* role_map, siz
     p.mma_b = mma_b;
     p.mma_out = mma_out;
     p.inner = inner;
+    p.budget_ns = 0;  // fixed work, as gplk_powervirus_launch with budget_ns = 0
     const int grid = blocks > 0 ? blocks : d.sm_count;
     pv::pv_kernel<<<grid, pv::kThreads, smem, stream>>>(p);
     return launch_status(cudaGetLastError());

@@ -53,6 +53,7 @@ class PvCfg(ctypes.Structure):
         ("mma_out", _p),
         ("blocks", _i),
         ("inner", _i),
+        ("budget_ns", ctypes.c_ulonglong),
     ]
 
 

@@ -225,6 +225,17 @@ int gpl_workload_powervirus_run(gpl_workload_ctx_t *ctx) {
     cfg.sink = d_sink;
     cfg.blocks = sm_count;
     cfg.inner = inner;
+    // Each role does exactly `inner` units per launch, as in the reference.
+    // GPL_PV_BUDGET_US (fixed-time rungs only) instead time-boxes each launch:
+    // every role keeps working until the budget has passed, so no unit idles
+    // behind the slowest one. An always-ready FFMA warp can then crowd the
+    // single MMA-issuing thread off its scheduler, so the budget suits
+    // tensor-weighted mixes (e.g. tensor 2 : fma 1 : dram 1).
+    {
+        const char *bv = getenv("GPL_PV_BUDGET_US");
+        const double us = bv ? atof(bv) : 0.0;
+        cfg.budget_ns = (!fixed_work && us > 0.0) ? (unsigned long long)(us * 1e3) : 0ull;
+    }
 
 #define PV_KERNEL(nb, s)                                                                  \
     do {                                                                                  \

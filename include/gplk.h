@@ -37,7 +37,7 @@ typedef enum {
 const char *gplk_status_string(int status);
 
 /* ABI version: bumped when a signature or a data layout changes. */
-int gplk_abi_version(void);
+int gplk_abi_version(void);  /* 2: gplk_pv_cfg.budget_ns */
 
 /* Reads the device status word of the current device (first error recorded
  * by any gplk kernel since the last clear) and the site that recorded it.
@@ -131,6 +131,10 @@ typedef struct {
     float *mma_out;                /* device or NULL: 128 x 256 F32 accumulator dump */
     int blocks;                    /* grid size; 0 = one block per SM */
     int inner;                     /* iterations of each role per launch */
+    unsigned long long budget_ns;  /* 0: fixed work (exactly `inner` per role);
+                                      else every role, after its fixed work,
+                                      keeps going until budget_ns after its
+                                      block started (uniform load) */
 } gplk_pv_cfg;
 
 /* One launch of the mixed-unit power kernel.

@@ -119,3 +119,21 @@ def test_ramp_block_counts(gplk, cuda):
         cfg, *_rest = _setup(gplk, cuda, [1, 1, 1, 0, 0, 0, 0, 0], inner=64, blocks=nb, verify=False)
         gplk.powervirus_launch(cfg)
     torch.cuda.synchronize()
+
+
+def test_time_boxed_launch_runs_to_its_budget(gplk, cuda):
+    """With budget_ns set, every role keeps working until the deadline: a
+    launch with a tiny fixed part lasts at least the budget, and stays clean."""
+    import torch
+
+    cfg, *_rest = _setup(gplk, cuda, [1, 1, 1, 1, 1, 1, 1, 1], inner=8, verify=False)
+    cfg.budget_ns = 3_000_000
+    gplk.powervirus_launch(cfg)  # warm-up
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    gplk.powervirus_launch(cfg)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    assert 2.9 <= ms <= 50.0, ms
