@@ -61,6 +61,10 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--mix", default="4,1,2", help="powervirus role weights tensor,fma,dram[,sfu,int32,smem,l2,atomic]")
+    ap.add_argument("--budget-us", type=float, default=1000.0, help="powervirus launch time box")
+    ap.add_argument("--duty-on-ms", type=float, default=100.0)
+    ap.add_argument("--duty-off-ms", type=float, default=100.0)
     ap.add_argument("--elements", type=int, default=TRIAD_N,
                     help="memstream array length (smaller cases are for profiling only)")
     return ap.parse_args()
@@ -69,10 +73,14 @@ def parse_args():
 # ------------------------------------------------------------ distributed plumbing
 
 class Dist:
-    def __init__(self, n_gpus: int):
+    """One process per GPU (torchrun env). NCCL on the GPU box; `backend`
+    "gloo" runs the same barrier / max-over-ranks logic on CPU ranks."""
+
+    def __init__(self, n_gpus: int, backend: str = "nccl"):
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.backend = backend
         self.pg = None
         if self.world > 1:
             import datetime
@@ -80,26 +88,41 @@ class Dist:
             import torch
             import torch.distributed as dist
 
-            torch.cuda.set_device(self.local)
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                    device_id=torch.device("cuda", self.local))
+            kw = {}
+            if backend == "nccl":
+                torch.cuda.set_device(self.local)
+                kw["device_id"] = torch.device("cuda", self.local)
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120), **kw)
             self.pg = dist
+
+    def _dev(self):
+        return "cuda" if self.backend == "nccl" else "cpu"
 
     def barrier(self):
         if self.pg:
             import torch
 
-            t = torch.zeros(1, device="cuda")
+            t = torch.zeros(1, device=self._dev())
             self.pg.all_reduce(t)
-            torch.cuda.synchronize()
+            if self.backend == "nccl":
+                torch.cuda.synchronize()
 
     def max(self, x: float) -> float:
         if not self.pg:
             return x
         import torch
 
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        t = torch.tensor([x], dtype=torch.float64, device=self._dev())
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, x: float) -> float:
+        if not self.pg:
+            return x
+        import torch
+
+        t = torch.tensor([x], dtype=torch.float64, device=self._dev())
+        self.pg.all_reduce(t)
         return float(t.item())
 
     def close(self):
@@ -119,8 +142,9 @@ REASONS = {
 class ClockSampler:
     """NVML sampling thread: SM clock, throttle reasons and power, every 25 ms."""
 
-    def __init__(self, device_index: int):
+    def __init__(self, device_index: int, period_s: float = 0.025):
         self.idx = device_index
+        self.period = period_s
         self.samples = []
         self._stop = threading.Event()
         self._thr = None
@@ -154,7 +178,7 @@ class ClockSampler:
                 self._sample()
             except Exception:
                 pass
-            self._stop.wait(0.025)
+            self._stop.wait(self.period)
 
     def start(self):
         if self.ok:
@@ -446,6 +470,96 @@ def bench_gemm(args, dist: Dist) -> dict:
     }
 
 
+# ------------------------------------------------------------ powervirus rung
+
+def bench_powervirus(args, dist: Dist) -> dict:
+    """Duty-cycled powervirus on every GPU in phase; each cycle = burst of
+    time-boxed launches for duty_on_ms, a 256 MiB BF16 allreduce across all
+    ranks (NCCL; skipped at N=1), then duty_off_ms idle. One step = one
+    cycle. NVML power is sampled every 10 ms and split into burst and idle
+    windows."""
+    import torch
+    import gplk
+    from gplk import rung
+
+    dev = torch.device("cuda", dist.local)
+    torch.cuda.set_device(dev)
+    gplk.lib()
+    weights = [int(x) for x in args.mix.split(",")]
+    weights += [0] * (8 - len(weights))
+    m, counts = gplk.pv_role_map(weights)
+    role_map = torch.tensor(m, dtype=torch.uint8, device=dev)
+    buf = torch.full((2 << 30,), 0x3C, dtype=torch.uint8, device=dev)  # 2 GiB streaming buffer
+    sink = torch.zeros(1 + 1024, dtype=torch.float32, device=dev)
+    cfg = gplk.PvCfg()
+    cfg.role_map = role_map.data_ptr()
+    cfg.stream_buf = buf.data_ptr()
+    cfg.stream_bytes = buf.numel()
+    cfg.sink = sink.data_ptr()
+    cfg.blocks = 0
+    cfg.inner = 256
+    cfg.budget_ns = int(args.budget_us * 1e3)
+    stream = torch.cuda.current_stream(dev)
+    ar = torch.ones((128 << 20,), dtype=torch.bfloat16, device=dev)  # 256 MiB
+    ar_bytes = ar.numel() * 2
+
+    def launch():
+        gplk.powervirus_launch(cfg, stream=stream)
+
+    def sync():
+        torch.cuda.synchronize(dev)
+
+    allreduce = (lambda: dist.pg.all_reduce(ar)) if dist.world > 1 else None
+    on_ms, off_ms = args.duty_on_ms, args.duty_off_ms
+    rung.run_duty_cycles(max(args.warmup, 3), on_ms, off_ms, launch, sync, allreduce, barrier=dist.barrier)
+    sampler = ClockSampler(dist.local, period_s=0.01)
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist.barrier()
+    e0.record(stream)
+    log = rung.run_duty_cycles(args.steps, on_ms, off_ms, launch, sync, allreduce, barrier=dist.barrier)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    sampler.stop()
+    code, site = gplk.status_read()
+    if code != 0:
+        raise RuntimeError(f"device status {code} at {site:#x}")
+    ms_max = dist.max(e0.elapsed_time(e1))
+    samples = [(t, w) for (t, _sm, _r, w) in sampler.samples]
+    burst = rung.window_power(samples, list(zip(log.burst_start, log.burst_end)))
+    idle = rung.window_power(samples, [(f + 0.02, c) for f, c in zip(log.fabric_end, log.cycle_end)])
+    limit = sampler.limit_w or 1000.0
+    burst_w = sum(burst) / len(burst) if burst else 0.0
+    idle_w = sum(idle) / len(idle) if idle else 0.0
+    pct = 100.0 * burst_w / limit
+    pct_mean = dist.sum(pct) / dist.world
+    node_burst_w = dist.sum(burst_w)
+    fabric_s = sorted(log.fabric_s)[len(log.fabric_s) // 2] if log.fabric_s else 0.0
+    clocks = sampler.summary()
+    return {
+        "metric": "powervirus burst power % of enforced limit", "value": round(pct_mean, 2), "unit": "%",
+        "n_gpus": dist.world, "steps": args.steps, "warmup": max(args.warmup, 3),
+        "ms_per_step": round(ms_max / args.steps, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "e4m3+f32", "data": "synthetic: 0x3c-filled 2 GiB stream, E4M3 1.0 tiles",
+        "config": {"workload": "powervirus duty cycle: in-kernel tcgen05 FP8 + FFMA + TMA-bulk HBM streaming; "
+                               f"{on_ms:g} ms on / {off_ms:g} ms off; 256 MiB BF16 allreduce per cycle",
+                   "mix_tensor_fma_dram_sfu_int32_smem_l2_atomic": weights, "warps_per_64": counts,
+                   "launch_budget_us": args.budget_us,
+                   "parallelism": f"replicas x{dist.world} in phase, NCCL allreduce per cycle"},
+        "power": {"burst_avg_w": round(burst_w, 1), "idle_avg_w": round(idle_w, 1),
+                  "swing_w": round(max(burst or [0]) - min(idle or [0]), 1) if burst and idle else None,
+                  "burst_max_w": round(max(burst), 1) if burst else None,
+                  "node_burst_sum_w": round(node_burst_w, 1), "enforced_limit_w": limit,
+                  "samples_burst": len(burst), "samples_idle": len(idle)},
+        "fabric": {"allreduce_bytes": ar_bytes if allreduce else 0, "median_s": round(fabric_s, 6),
+                   "busbw_gbs": round(rung.allreduce_busbw_gbs(ar_bytes, fabric_s, dist.world), 1)
+                   if allreduce else None},
+        "clocks": clocks,
+        "gpu_launches": int(sum(log.launches)),
+    }
+
+
 # ------------------------------------------------------------ reference arm
 
 def bench_reference(args, dist: Dist) -> dict | None:
@@ -501,7 +615,7 @@ def main():
         elif args.workload in ("sgemm", "fp8", "nvfp4"):
             line = bench_gemm(args, dist)
         else:
-            raise SystemExit("powervirus: not a bench.py workload yet")
+            line = bench_powervirus(args, dist)
         if dist.rank == 0 and dist.world == 1 and not args.no_cpu and args.workload == "memstream":
             line["cpu_baseline"] = cpu_triad_gbps(args.cpu_seconds)
         if dist.rank == 0:

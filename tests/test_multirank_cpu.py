@@ -1,0 +1,78 @@
+"""Multi-rank host logic on CPU ranks (gloo, world size 2): the bench's
+barrier and max-over-ranks timing, and the duty-cycle loop with its
+per-cycle allreduce (the fabric step), run in phase on every rank."""
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch.multiprocessing as mp
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank: int, world: int, port: int, out):
+    os.environ.update({"RANK": str(rank), "WORLD_SIZE": str(world), "LOCAL_RANK": str(rank),
+                       "MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port)})
+    import sys
+    from pathlib import Path
+
+    repo = Path(__file__).resolve().parent.parent
+    sys.path[:0] = [str(repo), str(repo / "gpu-power-lab_b200")]
+    import torch
+
+    import bench
+    from gplk import rung
+
+    d = bench.Dist(world, backend="gloo")
+    d.barrier()
+    mx = d.max(float(rank + 1) * 1.5)
+    tot = d.sum(1.0)
+    buf = torch.full((1 << 16,), float(rank + 1))
+    launches = []
+
+    def allreduce():
+        d.pg.all_reduce(buf)
+
+    log = rung.run_duty_cycles(cycles=4, on_ms=20, off_ms=10, launch=lambda: launches.append(1), sync=lambda: None,
+                               allreduce=allreduce, barrier=d.barrier)
+    d.close()
+    out.put((rank, mx, tot, float(buf[0]), len(log.burst_start), min(log.launches), sum(launches)))
+
+
+def test_two_cpu_ranks_barrier_max_and_fabric_cycles():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, mx, tot, val, cycles, min_launch, total in res:
+        assert mx == 3.0 and tot == 2.0
+        # four cycles, each ending with an allreduce of a buffer that starts
+        # at (rank + 1): after k rounds every element is 3 * 2^(k-1)
+        assert cycles == 4
+        assert val == 3.0 * 2 ** 3
+        assert min_launch > 0 and total >= 4
+
+
+def test_busbw_and_windows():
+    import sys
+    from pathlib import Path
+
+    sys.path.insert(0, str(Path(__file__).resolve().parent.parent / "gpu-power-lab_b200"))
+    from gplk import rung
+
+    assert rung.allreduce_busbw_gbs(256 << 20, 1.0, 1) == 0.0
+    assert rung.allreduce_busbw_gbs(1_000_000_000, 1.0, 8) == pytest.approx(1.75)
+    samples = [(0.5, 100.0), (1.5, 900.0), (2.5, 200.0), (3.2, 950.0)]
+    assert rung.window_power(samples, [(1.0, 2.0), (3.0, 4.0)]) == [900.0, 950.0]
