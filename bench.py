@@ -157,6 +157,9 @@ class ClockSampler:
             self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
             self.max_sm = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
             self.limit_w = pynvml.nvmlDeviceGetEnforcedPowerLimit(self.h) / 1000.0
+            # Instantaneous power (NVML_FI_DEV_POWER_INSTANT) where the driver
+            # has it: the averaged reading smears a 100 ms square wave.
+            self.instant_ok = hasattr(pynvml, "NVML_FI_DEV_POWER_INSTANT")
             self.ok = True
         except Exception:
             self.max_sm = None
@@ -169,8 +172,18 @@ class ClockSampler:
             reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
         except Exception:
             reasons = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
-        power = nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0
-        self.samples.append((time.time(), sm, reasons, power))
+        power = nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0  # driver-averaged
+        inst = None
+        if self.instant_ok:
+            try:
+                fv = nv.nvmlDeviceGetFieldValues(self.h, [nv.NVML_FI_DEV_POWER_INSTANT])[0]
+                if fv.nvmlReturn == 0:  # milliwatts; the value type varies by driver
+                    vt = int(fv.valueType)
+                    raw = fv.value.uiVal if vt == 1 else (fv.value.ulVal if vt == 2 else fv.value.ullVal)
+                    inst = raw / 1000.0
+            except Exception:
+                self.instant_ok = False
+        self.samples.append((time.time(), sm, reasons, inst if inst is not None else power))
 
     def _run(self):
         while not self._stop.is_set():
