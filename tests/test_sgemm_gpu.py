@@ -34,7 +34,8 @@ def test_sgemm_1024_seed0(gplk, oracle, cuda):
 
 
 @pytest.mark.parametrize("mnk", [(1, 1, 1), (33, 17, 5), (100, 130, 257), (257, 129, 1000),
-                                 (64, 64, 16), (128, 256, 64), (2048, 512, 300), (3000, 2000, 128)])
+                                 (64, 64, 16), (128, 256, 64), (2048, 512, 300), (3000, 2000, 128),
+                                 (1000, 1000, 333), (768, 1024, 1024), (1024, 2048, 4096)])
 def test_sgemm_shapes(mnk, gplk, oracle, cuda):
     M, N, K = mnk
     A = oracle.uniform_f32(M * K, seed=M, lo=-1.0, hi=1.0).reshape(M, K)
