@@ -39,7 +39,7 @@ TRIAD_BYTES = 12 * TRIAD_N  # read b, read c, write a (runner/src/workload_util.
 # dram__bytes_read.sum + dram__bytes_write.sum per launch from ncu captures
 # (profiles/*.md, scaled to the full launch where the capture was smaller).
 NCU_TRAFFIC = {
-    "memstream": 12.59e9,  # profiles/memstream_triad_2p30.md: 8 x 1.574 GB (3 x 2^27 capture)
+    "memstream": 12.58e9,  # profiles/memstream_triad_2p30.md: 8 x 1.573 GB (3 x 2^27 capture)
     "sgemm": None,
     "fp8": None,
     "nvfp4": None,
@@ -56,7 +56,7 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["memstream", "sgemm", "fp8", "nvfp4", "powervirus"],
                     default="memstream")
-    ap.add_argument("--kernel", choices=["vec4", "bulk"], default="vec4",
+    ap.add_argument("--kernel", choices=["vec4", "bulk"], default="bulk",
                     help="memstream kernel variant")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
