@@ -39,10 +39,11 @@ TRIAD_BYTES = 12 * TRIAD_N  # read b, read c, write a (runner/src/workload_util.
 # dram__bytes_read.sum + dram__bytes_write.sum per launch from ncu captures
 # (profiles/*.md, scaled to the full launch where the capture was smaller).
 NCU_TRAFFIC = {
-    "memstream": 12.58e9,  # profiles/memstream_triad_2p30.md: 8 x 1.573 GB (3 x 2^27 capture)
-    "sgemm": None,
-    "fp8": None,
-    "nvfp4": None,
+    "memstream_vec4": 12.58e9,  # profiles/memstream_triad_2p30.md: 8 x 1.573 GB (3 x 2^27 capture)
+    "memstream_bulk": 12.58e9,  # profiles/memstream_triad_2p30.md: 8 x 1.572 GB (3 x 2^27 capture)
+    "sgemm": 8.4e6,             # profiles/sgemm_f32_1024.md
+    "fp8": 356.7e6,             # profiles/gemm_fp8_8192.md
+    "nvfp4": 1343.6e6,          # profiles/gemm_nvfp4_16384.md
 }
 
 NOMINAL_TFLOPS = {"fp8": 4500.0, "nvfp4": 9000.0, "sgemm": 148 * 128 * 2 * 1.965e9 / 1e12}
@@ -317,7 +318,7 @@ def bench_memstream(args, dist: Dist) -> dict:
     else:
         workload = "memstream STREAM triad a = b + 3.0*c, FP32, 3 x 2^30 elements (4 GiB each)"
 
-    traffic = NCU_TRAFFIC["memstream"]
+    traffic = NCU_TRAFFIC["memstream_bulk" if bulk else "memstream_vec4"] if n == TRIAD_N else None
     out = {
         "metric": "memstream triad GB/s",
         "value": round(value, 2),
