@@ -140,3 +140,28 @@ extern "C" int gplk_status_read(int* code, int* site, int clear) {
     }
     return GPLK_STATUS_OK;
 }
+
+// ------------------------------------------------------------ watchdog self-test
+namespace gplk {
+// One block waits on an mbarrier that nothing ever arrives on. The bounded
+// wait must give up after budget_ns, record GPLK_STATUS_DEVICE_TIMEOUT with
+// site 0x0F01 and let the block exit normally.
+__global__ void selftest_wait_kernel(uint64_t budget_ns, int* gave_up) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_flag = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+    const bool ok = mbar_wait(&bar, 0, &abort_flag, 0x0F01, budget_ns);
+    if (threadIdx.x == 0 && gave_up) *gave_up = ok ? 0 : 1;
+}
+}  // namespace gplk
+
+extern "C" int gplk_selftest_wait_timeout(unsigned long long budget_ns, int* gave_up, cudaStream_t stream) {
+    if (budget_ns == 0 || budget_ns > 2000000000ull) return GPLK_STATUS_BAD_ARG;
+    gplk::selftest_wait_kernel<<<1, 32, 0, stream>>>(budget_ns, gave_up);
+    return gplk::launch_status(cudaGetLastError());
+}

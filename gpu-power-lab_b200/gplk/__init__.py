@@ -88,6 +88,8 @@ def lib() -> ctypes.CDLL:
     L.gplk_gemm_fp8_tn.argtypes = [_p, _p, _p, _i, _i, _i, _p, _p, _p]
     L.gplk_gemm_nvfp4_tn.restype = _i
     L.gplk_gemm_nvfp4_tn.argtypes = [_p, _p, _p, _p, _p, _i, _i, _i, _p, _p]
+    L.gplk_selftest_wait_timeout.restype = _i
+    L.gplk_selftest_wait_timeout.argtypes = [ctypes.c_ulonglong, _p, _p]
     L.gplk_nvfp4_sf_bytes.restype = _sz
     L.gplk_nvfp4_sf_bytes.argtypes = [_i, _i]
     if hasattr(L, "gplk_powervirus_launch"):
@@ -123,6 +125,13 @@ def status_read(clear: bool = True) -> tuple[int, int]:
     code, site = _i(0), _i(0)
     _check("gplk_status_read", lib().gplk_status_read(ctypes.byref(code), ctypes.byref(site), int(clear)))
     return code.value, site.value
+
+
+def selftest_wait_timeout(budget_ns: int, gave_up=None, stream=None) -> None:
+    """Launch the watchdog self-test: a wait that can never complete gives up
+    after budget_ns and records a device-wait timeout (see include/gplk.h)."""
+    _check("gplk_selftest_wait_timeout", lib().gplk_selftest_wait_timeout(
+        budget_ns, gave_up.data_ptr() if gave_up is not None else None, _stream(stream)))
 
 
 # ------------------------------------------------------------ memstream

@@ -23,6 +23,7 @@
 #include <string.h>
 
 #include "gemm_lt.h"
+#include "gpl_fault.h"
 #include "gplk.h"
 #include "util.h"
 
@@ -107,6 +108,12 @@ int gpl_workload_gemm_run(gpl_workload_ctx_t *ctx) {
         }                                                                           \
     } while (0)
 
+    if (gpl_fault_is("alloc")) {
+        ctx->error = GPL_FAULT_ALLOC_MSG;
+        gpl_errf("gemm: %s", ctx->error);
+        rc = -1;
+        goto cleanup;
+    }
     for (int i = 0; i < ns; i++) G_CUDA(cudaStreamCreateWithFlags(&st[i], cudaStreamNonBlocking));
 
     if (path == PATH_GPLK_LT) {
@@ -167,6 +174,12 @@ int gpl_workload_gemm_run(gpl_workload_ctx_t *ctx) {
         }                                                                                               \
     } while (0)
 
+    if (gpl_fault_is("launch")) {
+        ctx->error = GPL_FAULT_LAUNCH_MSG;
+        gpl_errf("gemm: %s", ctx->error);
+        rc = -1;
+        goto cleanup;
+    }
     for (int i = 0; i < ns; i++) ONE_GEMM(i); /* prime */
     G_CUDA(cudaDeviceSynchronize());
 

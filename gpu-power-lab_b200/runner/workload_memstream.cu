@@ -17,6 +17,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include "gpl_fault.h"
 #include "gplk.h"
 #include "util.h"
 
@@ -64,6 +65,12 @@ int gpl_workload_memstream_run(gpl_workload_ctx_t *ctx) {
         return -1;
     }
 
+    if (gpl_fault_is("alloc")) {
+        ctx->error = GPL_FAULT_ALLOC_MSG;
+        gpl_errf("memstream: %s", ctx->error);
+        rc = -1;
+        goto cleanup;
+    }
     MS_CUDA(cudaMalloc((void **)&dA, bytes));
     MS_CUDA(cudaMalloc((void **)&dB, bytes));
     MS_CUDA(cudaMemset(dA, 0x3c, bytes));
@@ -76,6 +83,12 @@ int gpl_workload_memstream_run(gpl_workload_ctx_t *ctx) {
 
 #define LAUNCH(i) MS_GPLK(bulk ? gplk_triad_f32_bulk(dC[i], dA, dB, scalar, n, st[i]) \
                                : gplk_triad_f32(dC[i], dA, dB, scalar, n, st[i]))
+    if (gpl_fault_is("launch")) {
+        ctx->error = GPL_FAULT_LAUNCH_MSG;
+        gpl_errf("memstream: %s", ctx->error);
+        rc = -1;
+        goto cleanup;
+    }
     for (int i = 0; i < ns; i++) LAUNCH(i);  /* prime */
     MS_CUDA(cudaDeviceSynchronize());
 

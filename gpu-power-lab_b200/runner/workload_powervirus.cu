@@ -23,6 +23,7 @@
 #include <time.h>
 
 #include "gemm_lt.h"
+#include "gpl_fault.h"
 #include "gplk.h"
 #include "util.h"
 
@@ -175,6 +176,7 @@ int gpl_workload_powervirus_run(gpl_workload_ctx_t *ctx) {
     memset(&cfg, 0, sizeof(cfg));
     PV_CHECK(st != NULL, "oom (streams)");
 
+    PV_CHECK(!gpl_fault_is("alloc"), GPL_FAULT_ALLOC_MSG);
     PV_CUDA(cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, a->device));
     PV_CUDA(cudaMemGetInfo(&freeb, &totalb));
     buf_bytes = freeb / 4;
@@ -245,6 +247,7 @@ int gpl_workload_powervirus_run(gpl_workload_ctx_t *ctx) {
     } while (0)
 #define PV_TENSOR(count) PV_CHECK(tensor_stream_enqueue(&ts, (count)) == 0, "tensor stream enqueue failed")
 
+    PV_CHECK(!gpl_fault_is("launch"), GPL_FAULT_LAUNCH_MSG);
     gpl_telemetry_set_phase(ctx->tele, GPL_PHASE_WARMUP);
     t_start = gpl_mono_ns();
     warmup_ns = (uint64_t)(a->warmup_sec * 1e9);

@@ -44,6 +44,13 @@ int gplk_abi_version(void);  /* 2: gplk_pv_cfg.budget_ns */
  * Synchronises the current device. If clear != 0 the word is reset to OK. */
 int gplk_status_read(int *code, int *site, int clear);
 
+/* Watchdog self-test (no counterpart in the reference, which has no bounded
+ * waits): one block waits on a barrier that nothing completes, gives up after
+ * budget_ns (at most 2 s), writes 1 to *gave_up (device pointer, may be NULL)
+ * and records GPLK_STATUS_DEVICE_TIMEOUT, site 0x0F01, in the status word.
+ * The context stays usable. For tests of the failure path. */
+int gplk_selftest_wait_timeout(unsigned long long budget_ns, int *gave_up, cudaStream_t stream);
+
 /* ------------------------------------------------------------ memstream
  * STREAM triad a[i] = b[i] + s * c[i] in FP32, computed as one fused
  * multiply-add fmaf(s, c[i], b[i]) per element, so the result is bit-exact

@@ -45,7 +45,7 @@ nvcc $GEN -o "$OUT/gpu-power-runner" "$TMP"/ref/*.o $LIBS
 
 # 2. kept host + drop-ins + libgplk.so (this tree's include/ shadows gemm_lt.h)
 mkdir -p "$TMP/gplk"
-INC="-I$REPO/include -I$SRC"
+INC="-I$REPO/include -I$DROP -I$SRC"
 for f in $KEPT_C; do
     gcc $CFLAGS -I"$SRC" -c "$SRC/$f" -o "$TMP/gplk/${f%.c}.o"
 done

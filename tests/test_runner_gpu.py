@@ -128,3 +128,21 @@ def test_memstream_beats_reference_runner(tmp_path):
     _ok(res_g, s_g)
     print(f"memstream GB/s: reference {s_r['throughput']['value']:.0f}, drop-in {s_g['throughput']['value']:.0f}")
     assert s_g["throughput"]["value"] > s_r["throughput"]["value"]
+
+
+@needs_runner
+@pytest.mark.parametrize("op", ["memstream", "sgemm", "powervirus"])
+def test_injected_alloc_failure_maps_to_oom(op, tmp_path):
+    """Host-side fault injection (GPL_FAULT=alloc): the runner reports result
+    "oom" and exits 5, with no GPU fault involved."""
+    res, s, _ = run_rung(GPLK_RUNNER, tmp_path, "--op", op, "--size", "1024", env={"GPL_FAULT": "alloc"})
+    assert res.returncode == 5
+    assert s["result"] == "oom" and "injected" in s.get("error_message", "")
+
+
+@needs_runner
+@pytest.mark.parametrize("op", ["memstream", "sgemm", "powervirus"])
+def test_injected_launch_failure_maps_to_cuda_error(op, tmp_path):
+    res, s, _ = run_rung(GPLK_RUNNER, tmp_path, "--op", op, "--size", "1024", env={"GPL_FAULT": "launch"})
+    assert res.returncode == 5
+    assert s["result"] == "cuda_error" and "injected" in s.get("error_message", "")
