@@ -4,10 +4,10 @@
 #   gpu-power-runner        the unmodified reference runner (all of
 #                           runner/src), for same-box comparisons
 #   gpu-power-runner-gplk   the reference's kept host (main, args, telemetry,
-#                           summary, probe, util, fft, observe, nccl) with
-#                           this repository's drop-ins for the load
-#                           generators (gpu-power-lab_b200/runner/*.c|cu,
-#                           include/gemm_lt.h) linked to libgplk.so
+#                           probe, util, fft, observe, nccl) with this
+#                           repository's drop-ins for the load generators and
+#                           the summary emitter (gpu-power-lab_b200/runner/
+#                           *.c|cu, include/gemm_lt.h) linked to libgplk.so
 # TEST INFRASTRUCTURE: the integration tests run both. Neither binary
 # touches power limits or clocks unless given --power-limit,
 # --raise-power-limit or --lock-clocks, which the tests never pass.
@@ -31,11 +31,11 @@ GEN="-gencode arch=compute_100a,code=sm_100a"
 CFLAGS="-std=gnu11 -O2 -Wall -Wno-unused-parameter -DGPL_HAVE_NCCL -I$CUDA/include"
 NVFLAGS="$GEN -O3 -std=c++17 -DGPL_HAVE_NCCL"
 LIBS="-L$CUDA/lib64 -L$CUDA/lib64/stubs -lcublas -lcublasLt -lcufft -lnvidia-ml -lnccl -lpthread -lm"
-KEPT_C="main.c args.c telemetry.c probe.c workload_observe.c workload_fft.c summary.c util.c"
+KEPT_C="main.c args.c telemetry.c probe.c workload_observe.c workload_fft.c util.c"
 
 # 1. the reference as it is
 mkdir -p "$TMP/ref"
-for f in $KEPT_C workload_gemm.c workload_util.c; do
+for f in $KEPT_C summary.c workload_gemm.c workload_util.c; do
     gcc $CFLAGS -I"$SRC" -c "$SRC/$f" -o "$TMP/ref/${f%.c}.o"
 done
 for f in workload_memstream.cu workload_powervirus.cu gemm_lt.cu workload_nccl.cu; do
@@ -50,7 +50,7 @@ for f in $KEPT_C; do
     gcc $CFLAGS -I"$SRC" -c "$SRC/$f" -o "$TMP/gplk/${f%.c}.o"
 done
 nvcc $NVFLAGS -I"$SRC" -c "$SRC/workload_nccl.cu" -o "$TMP/gplk/workload_nccl.o"
-for f in workload_gemm.c workload_util.c; do
+for f in workload_gemm.c workload_util.c summary.c; do
     gcc $CFLAGS $INC -c "$DROP/$f" -o "$TMP/gplk/drop_${f%.c}.o"
 done
 for f in workload_memstream.cu workload_powervirus.cu; do

@@ -146,3 +146,31 @@ def test_injected_launch_failure_maps_to_cuda_error(op, tmp_path):
     res, s, _ = run_rung(GPLK_RUNNER, tmp_path, "--op", op, "--size", "1024", env={"GPL_FAULT": "launch"})
     assert res.returncode == 5
     assert s["result"] == "cuda_error" and "injected" in s.get("error_message", "")
+
+
+@needs_runner
+@pytest.mark.parametrize("op,prec,size", [("memstream", "fp32", "32768"), ("sgemm", "fp32", "1024"),
+                                          ("sgemm", "fp8", "8192")])
+def test_strict_summary_meets_version1_contract(op, prec, size, tmp_path):
+    """GPL_SUMMARY_SCHEMA=strict: the drop-in emitter writes the version-1
+    document (no efficiency / transient blocks) for rungs version 1 can name."""
+    from gplk import summary as S
+
+    res, s, _ = run_rung(GPLK_RUNNER, tmp_path, "--op", op, "--precision", prec, "--size", size,
+                         env={"GPL_SUMMARY_SCHEMA": "strict"})
+    _ok(res, s)
+    S.validate_doc(s, strict=True)
+    assert "efficiency" not in s and "transient" not in s
+
+
+@needs_runner
+def test_powervirus_summary_extended_contract_and_violation_units(tmp_path):
+    """The default summary meets the extended contract, and the power-cap
+    violation time is microseconds: never longer than the steady window."""
+    from gplk import summary as S
+
+    res, s, _ = run_rung(GPLK_RUNNER, tmp_path, "--op", "powervirus", "--size", "4096", "--duty-on-ms", "100",
+                         "--duty-off-ms", "100")
+    _ok(res, s)
+    S.validate_doc(s)
+    assert s["transient"]["power_violation_us"] <= s["timing"]["steady_ms"] * 1e3 * 1.05
