@@ -46,7 +46,13 @@ NCU_TRAFFIC = {
     "nvfp4": 1343.6e6,          # profiles/gemm_nvfp4_16384.md
 }
 
-NOMINAL_TFLOPS = {"fp8": 4500.0, "nvfp4": 9000.0, "sgemm": 148 * 128 * 2 * 1.965e9 / 1e12}
+NOMINAL_TFLOPS = {"fp8": 4500.0, "nvfp4": 9000.0, "sgemm": 148 * 128 * 2 * 1.965e9 / 1e12,
+                  "bf16": 2250.0, "f16": 2250.0, "tf32": 1125.0, "i8": 4500.0}
+# The dense cublasGemmEx precisions of the ladder (runner/src/workload_gemm.c:44-79), column-major NN.
+NN_GEMMS = {"bf16": ("bf16", "BF16 NN GEMM M=N=K=8192, FP32 accumulate, BF16 out"),
+            "f16": ("f16", "FP16 NN GEMM M=N=K=8192, FP32 accumulate, FP16 out"),
+            "tf32": ("tf32", "TF32 NN GEMM M=N=K=8192, FP32 in/out"),
+            "i8": ("s8", "INT8 NN GEMM M=N=K=8192, S32 accumulate and out")}
 
 
 def parse_args():
@@ -55,7 +61,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["memstream", "sgemm", "fp8", "nvfp4", "powervirus"],
+    ap.add_argument("--workload", choices=["memstream", "sgemm", "fp8", "nvfp4", "bf16", "f16", "tf32", "i8",
+                                           "powervirus"],
                     default="memstream")
     ap.add_argument("--kernel", choices=["vec4", "bulk"], default="bulk",
                     help="memstream kernel variant")
@@ -410,6 +417,23 @@ def bench_gemm(args, dist: Dist) -> dict:
 
         dtype, workload = "f32", "FP32 SGEMM C = A*B row-major, M=N=K=1024, U[-1,1)"
         launches_per_step = 2
+    elif w in NN_GEMMS:
+        n = 8192
+        if w == "i8":
+            A = torch.randint(-128, 128, (n, n), dtype=torch.int8, device=dev, generator=g)
+            B = torch.randint(-128, 128, (n, n), dtype=torch.int8, device=dev, generator=g)
+            D = torch.empty(n, n, dtype=torch.int32, device=dev)
+        else:
+            tdt = {"bf16": torch.bfloat16, "f16": torch.float16, "tf32": torch.float32}[w]
+            A = (torch.rand(n, n, device=dev, generator=g) * 2 - 1).to(tdt)
+            B = (torch.rand(n, n, device=dev, generator=g) * 2 - 1).to(tdt)
+            D = torch.empty(n, n, dtype=tdt, device=dev)
+
+        def step():
+            gplk.gemm_nn(w, A, B, D, n, n, n, stream=stream)
+
+        dtype, workload = NN_GEMMS[w]
+        launches_per_step = 1
     else:
         n = 8192 if w == "fp8" else 16384
         if w == "fp8":
@@ -478,7 +502,7 @@ def bench_gemm(args, dist: Dist) -> dict:
                    "parallelism": f"replicas x{dist.world}"},
         "roofline": {"bound": "tensor" if w != "sgemm" else "fp32-simt", "achieved": round(achieved, 1),
                      "peak": round(peak, 1), "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
-                     "traffic": NCU_TRAFFIC[w], "peak_source": "nominal dense"},
+                     "traffic": NCU_TRAFFIC.get(w), "peak_source": "nominal dense"},
         "clocks": sampler.summary(),
         "gpu_launches": args.steps * (1 if w != "sgemm" else 1),
     }
@@ -634,7 +658,7 @@ def main():
     try:
         if args.workload == "memstream":
             line = bench_memstream(args, dist)
-        elif args.workload in ("sgemm", "fp8", "nvfp4"):
+        elif args.workload in ("sgemm", "fp8", "nvfp4") or args.workload in NN_GEMMS:
             line = bench_gemm(args, dist)
         else:
             line = bench_powervirus(args, dist)

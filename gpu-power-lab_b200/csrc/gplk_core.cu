@@ -77,7 +77,8 @@ static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 // Box of box_rows x box_bytes with 128-byte swizzle (box_bytes <= 128).
 // Out-of-range elements of a box are filled with zeros by the TMA unit.
 static int encode_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t row_bytes, uint64_t rows,
-                             uint64_t pitch, uint32_t box_bytes, uint32_t box_rows) {
+                             uint64_t pitch, uint32_t box_bytes, uint32_t box_rows,
+                             CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
     auto enc = tensor_map_encoder();
     if (!enc) return GPLK_STATUS_UNSUPPORTED;
     cuuint64_t dims[2] = {row_bytes, rows};
@@ -85,7 +86,7 @@ static int encode_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t row_by
     cuuint32_t box[2] = {box_bytes, box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
-                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? GPLK_STATUS_OK : GPLK_STATUS_BAD_ARG;
 }
@@ -101,6 +102,21 @@ static int encode_tmap_2d_u16(CUtensorMap* map, const void* base, uint64_t inner
     cuuint32_t box[2] = {box_inner, box_outer};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? GPLK_STATUS_OK : GPLK_STATUS_BAD_ARG;
+}
+
+// The same for 32-bit elements (TMA stores of FP32 / S32 tiles).
+static int encode_tmap_2d_u32(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                              uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_outer) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return GPLK_STATUS_UNSUPPORTED;
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {pitch_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(base), dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? GPLK_STATUS_OK : GPLK_STATUS_BAD_ARG;

@@ -1,0 +1,537 @@
+// gplk_gemm_pair.cu - tcgen05 GEMMs on CTA pairs, one kernel template for
+// every dense precision of the GEMM ladder:
+//
+//   FP8   E4M3 x E4M3 -> FP32 accumulate -> scaled BF16  kind::f8f6f4, K = 32 / MMA
+//         cuBLASLt's TN layout (runner/src/gemm_lt.cu:98-132): A and B
+//         K-major, per-tensor FP32 scales
+//   BF16  BF16 x BF16 -> FP32 accumulate -> BF16   kind::f16,  K = 16 / MMA
+//   FP16  FP16 x FP16 -> FP32 accumulate -> FP16   kind::f16,  K = 16 / MMA
+//   TF32  FP32 x FP32 (TF32 products) -> FP32       kind::tf32, K =  8 / MMA
+//   INT8  S8 x S8 -> S32 accumulate -> S32          kind::i8,   K = 32 / MMA
+//         the last four in the layout of the reference's cublasGemmEx rung
+//         (runner/src/workload_gemm.c:44-79 maps them, :155-163 calls them):
+//         all matrices column-major, C = A * B with no transposes, alpha 1,
+//         beta 0. Column-major A (M x K) has M contiguous, so the MMA reads
+//         it MN-major; column-major B (K x N) is K-major. The reference
+//         computes FP16 with CUBLAS_COMPUTE_16F; here FP16 accumulates in
+//         FP32 (at least as accurate) and rounds once to FP16.
+// D is always M x N column-major.
+//
+// A persistent grid of 2-CTA clusters walks 256 x 256 output tiles in a
+// grouped order. Per cluster, one tcgen05.mma.cta_group::2 (M = 256,
+// N = 256) per 32 bytes of K; each CTA TMA-loads its own 128 rows of the A
+// tile and its own 128 rows (N) of the B tile with the 128-byte swizzle, no
+// cluster multicast. A pipeline stage holds two 128-byte slabs of K (64 KiB
+// per CTA, 8 MMAs), three stages deep: the leader's MMA thread waits on one
+// barrier and releases the stage in both CTAs with one commit per CTA every
+// 8 MMAs, not every 4. (On B200 the per-stage wait-and-commit sequence costs
+// tensor-pipe time: 4-MMA stages measured 3602 TFLOP/s for FP8 8192^3, 8-MMA
+// stages 4092.) The FP32/S32 accumulator is double-buffered in TMEM
+// (2 x 256 columns) so the epilogue of one tile overlaps the main loop of
+// the next. The epilogue converts, stages 8 KiB column chunks in shared
+// memory and writes them with TMA stores. Every wait is bounded (2 s); on
+// timeout the kernel records GPLK_STATUS_DEVICE_TIMEOUT with the site,
+// drains and returns.
+#include <cstring>
+
+#include "gplk_ptx.cuh"
+
+namespace gplk {
+namespace pair {
+
+enum class Kind { F8F6F4, F16, TF32, I8 };
+enum class Out { BF16, F16, F32, S32 };
+
+constexpr int kThreads = 192;
+constexpr int kSlab = 128 * 128;          // one CTA's 128 rows x 128 bytes of K
+constexpr int kSlabs = 2;                 // K slabs per stage (8 MMAs)
+constexpr int kStages = 3;
+constexpr int kOperandBytes = kSlabs * kSlab;    // A (or B) part of a stage: 32 KiB
+constexpr int kStageBytes = 2 * kOperandBytes;   // 64 KiB per CTA
+constexpr int kGroupM = 16;               // raster group along M (pair tiles)
+constexpr int kOutChunkBytes = 8192;      // epilogue staging: 8 KiB column chunks
+
+// Operand kind, A/B element format code in the instruction descriptor,
+// output type, A's major-ness (B is always K-major) and whether D is scaled
+// by per-tensor scales.
+template <Kind KIND, uint32_t FMT, Out OUT, bool A_KMAJOR = false, bool SCALED = false>
+struct Cfg {
+    static constexpr Kind kKind = KIND;
+    static constexpr Out kOut = OUT;
+    static constexpr bool kAKMajor = A_KMAJOR;
+    static constexpr bool kScaled = SCALED;
+    static constexpr int kInBytes = KIND == Kind::F16 ? 2 : KIND == Kind::TF32 ? 4 : 1;
+    static constexpr int kOutBytes = (OUT == Out::BF16 || OUT == Out::F16) ? 2 : 4;
+    static constexpr int kRowElems = 128 / kInBytes;  // elements per 128-byte run = K per stage
+    // MN-major A: the CTA's 128 rows of M are 128 / kRowElems runs of
+    // kRowElems elements; each run is one TMA box of kRowElems (M) x
+    // kRowElems (K) and one swizzle-atom column of the MMA's A operand.
+    static constexpr int kABoxes = A_KMAJOR ? 1 : 128 / kRowElems;
+    static constexpr uint32_t kABoxBytes = (uint32_t)kSlab / (uint32_t)kABoxes;
+    // One MMA consumes 32 bytes of K: 32 / kInBytes K rows of 128 bytes in
+    // the MN-major A tile, 32 bytes along each 128-byte row of B.
+    static constexpr uint32_t kAStep = (32u / (uint32_t)kInBytes) * 128u;
+    // Swizzle of the MN-major A tile. 16- and 8-bit operands use the 128-byte
+    // swizzle of 16-byte units (8-row, 1024-byte atoms). An MN-major TF32
+    // operand must use the 128-byte swizzle of 32-byte units instead (the
+    // MMA's SWIZZLE_128B_BASE32B layout, 4-row 512-byte atoms), which TMA
+    // writes with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B.
+    static constexpr bool kA32BAtoms = KIND == Kind::TF32;
+    static constexpr uint32_t kADescLayout = kA32BAtoms ? 1u : 2u;
+    static constexpr uint32_t kASbo = kA32BAtoms ? 512u : 1024u;
+    static constexpr int kChunkCols = kOutChunkBytes / (128 * kOutBytes);  // 32 or 16
+    static constexpr int kChunks = 256 / kChunkCols;
+    // Instruction descriptor (M = 256, N = 256, B K-major).
+    static constexpr uint32_t kIdesc = ((KIND == Kind::I8 ? 2u : 1u) << 4)  // D: S32 or F32
+                                       | (FMT << 7) | (FMT << 10)              // A, B formats
+                                       | ((A_KMAJOR ? 0u : 1u) << 15)          // A major-ness
+                                       | ((256u >> 3) << 17) | ((256u >> 4) << 24);
+};
+
+using CfgFP8 = Cfg<Kind::F8F6F4, 0u, Out::BF16, true, true>;  // F8F6F4 format 0 = E4M3
+using CfgBF16 = Cfg<Kind::F16, 1u, Out::BF16>;  // F16F32 format 1 = BF16
+using CfgF16 = Cfg<Kind::F16, 0u, Out::F16>;    // F16F32 format 0 = F16
+using CfgTF32 = Cfg<Kind::TF32, 2u, Out::F32>;  // F16F32 format 2 = TF32
+using CfgI8 = Cfg<Kind::I8, 1u, Out::S32>;      // S8 format 1 = signed
+
+template <Kind KIND>
+__device__ __forceinline__ void mma_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    if constexpr (KIND == Kind::F8F6F4) {
+        mma_pair_f8f6f4(d_tmem, a_desc, b_desc, idesc, accumulate);
+    } else if constexpr (KIND == Kind::F16) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+            "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+            : "memory");
+    } else if constexpr (KIND == Kind::TF32) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+            "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+            : "memory");
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+            "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+            : "memory");
+    }
+}
+
+// MN-major A tile: runs of 128 bytes along M, one K row per run, swizzle
+// atoms of `sbo` bytes along K (layout 2: 8 rows, 16-byte units; layout 1:
+// 4 rows, 32-byte units); the next run of M starts `lbo` bytes on.
+__device__ __forceinline__ uint64_t desc_mnmajor(uint32_t start, uint32_t lbo, uint32_t sbo, uint32_t layout) {
+    return smem_desc(start, lbo, sbo, layout);
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+struct Params {
+    void* D;
+    const float* scale_a;  // FP8: per-tensor scales (device pointers)
+    const float* scale_b;
+    int M, N, K;  // K in elements
+    int m_tiles, n_tiles, k_stages;
+    int tma_store;  // stage the epilogue through shared memory and TMA-store it
+};
+
+struct __align__(1024) Smem {
+    uint8_t stage[kStages][kStageBytes];
+    uint8_t out_stage[2][kOutChunkBytes];
+    uint64_t full[kStages];
+    uint64_t empty[kStages];
+    uint64_t acc_full[2];
+    uint64_t acc_empty[2];
+    uint64_t drain;
+    uint32_t tmem_base;
+    int abort;
+    int epi_fail;
+};
+
+__device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int& mt, int& nt) {
+    const int per_group = kGroupM * n_tiles;
+    const int group = t / per_group;
+    const int first_m = group * kGroupM;
+    const int gsize = min(m_tiles - first_m, kGroupM);
+    const int r = t % per_group;
+    mt = first_m + r % gsize;
+    nt = r / gsize;
+}
+
+template <int N>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[N]) {
+    if constexpr (N == 32) {
+        tmem_ld_32x32b_x32(taddr, r);
+    } else {
+        static_assert(N == 16, "16 or 32 columns per load");
+        tmem_ld_32x32b_x16(taddr, r);
+    }
+}
+
+template <class C>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmD, const Params p) {
+    constexpr int S = kStages;
+    extern __shared__ uint8_t smem_raw[];
+    Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    const uint32_t warp = warp_id_uniform();
+    const uint32_t lane = lane_id();
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int cluster = (int)(blockIdx.x >> 1);
+    const int nclusters = (int)(gridDim.x >> 1);
+    const int num_tiles = p.m_tiles * p.n_tiles;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i) {
+            mbar_init(&sm.full[i], 1);
+            mbar_init(&sm.empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&sm.acc_full[i], 1);
+            mbar_init(&sm.acc_empty[i], 8);  // four epilogue warps in each CTA of the pair
+        }
+        mbar_init(&sm.drain, 1);
+        sm.abort = 0;
+        sm.epi_fail = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+        if (p.tma_store) tma_prefetch_desc(&tmD);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(&sm.tmem_base, 512);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem = sm.tmem_base;
+
+    if (warp == 0) {
+        // TMA producer (one thread per CTA); both CTAs' bytes complete on the
+        // leader's `full` barrier.
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued_mask = 0, issued_parity = 0;
+            bool ok = true;
+            for (int t = cluster; t < num_tiles && ok; t += nclusters) {
+                int mt, nt;
+                tile_coords(t, p.m_tiles, p.n_tiles, mt, nt);
+                const int m_base = mt * 256 + (int)rank * 128;
+                for (int kb = 0; kb < p.k_stages; ++kb) {
+                    if (!mbar_wait_cluster(&sm.empty[stage], phase ^ 1u, &sm.abort, 0x0501)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* st = sm.stage[stage];
+                    const uint32_t full_leader = mapa_shared(smem_u32(&sm.full[stage]), 0);
+                    if (leader) mbar_arrive_expect_tx(&sm.full[stage], 2 * kStageBytes);
+#pragma unroll
+                    for (int sl = 0; sl < kSlabs; ++sl) {
+                        const int kk = kb * kSlabs + sl;  // 128-byte slab of K
+                        uint8_t* a_dst = st + sl * kSlab;
+                        if constexpr (C::kAKMajor) {
+                            tma_load_2d_pair(a_dst, &tmA, full_leader, kk * 128, m_base);
+                        } else {
+#pragma unroll
+                            for (int b = 0; b < C::kABoxes; ++b)
+                                tma_load_2d_pair(a_dst + b * C::kABoxBytes, &tmA, full_leader,
+                                                 (m_base + b * C::kRowElems) * C::kInBytes, kk * C::kRowElems);
+                        }
+                        tma_load_2d_pair(st + kOperandBytes + sl * kSlab, &tmB, full_leader, kk * 128,
+                                         nt * 256 + (int)rank * 128);
+                    }
+                    issued_mask |= 1u << stage;
+                    issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (leader && (!ok || sm.abort)) {
+                int dummy = 0;
+                for (int s2 = 0; s2 < S; ++s2)
+                    if (issued_mask & (1u << s2))
+                        mbar_wait_cluster(&sm.full[s2], (issued_parity >> s2) & 1u, &dummy, 0x0502, 100000000ull);
+            }
+        }
+    } else if (warp == 1) {
+        // MMA issuer: the leader's one thread.
+        if (leader && lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            for (int t = cluster; t < num_tiles && ok; t += nclusters) {
+                if (!mbar_wait_cluster(&sm.acc_empty[acc], acc_phase ^ 1u, &sm.abort, 0x0511)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem + (uint32_t)acc * 256u;
+                for (int kb = 0; kb < p.k_stages; ++kb) {
+                    if (!mbar_wait_cluster(&sm.full[stage], phase, &sm.abort, 0x0512)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(sm.stage[stage]);
+                    const uint32_t b_addr = a_addr + kOperandBytes;
+#pragma unroll
+                    for (int j = 0; j < 4 * kSlabs; ++j) {
+                        const uint32_t slab = (uint32_t)(j >> 2) * kSlab, jj = (uint32_t)(j & 3);
+                        const uint64_t a_desc =
+                            C::kAKMajor ? desc_kmajor_sw128(a_addr + slab + 32u * jj)
+                                        : desc_mnmajor(a_addr + slab + C::kAStep * jj, C::kABoxBytes, C::kASbo,
+                                                       C::kADescLayout);
+                        mma_pair<C::kKind>(d_tmem, a_desc, desc_kmajor_sw128(b_addr + slab + 32u * jj), C::kIdesc,
+                                           (kb | j) != 0);
+                    }
+                    const uint32_t e = smem_u32(&sm.empty[stage]);
+                    tc_commit_pair(mapa_shared(e, 0));
+                    tc_commit_pair(mapa_shared(e, 1));
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                const uint32_t f = smem_u32(&sm.acc_full[acc]);
+                tc_commit_pair(mapa_shared(f, 0));
+                tc_commit_pair(mapa_shared(f, 1));
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+            tc_commit_pair(mapa_shared(smem_u32(&sm.drain), 0));
+            int dummy = 0;
+            mbar_wait_cluster(&sm.drain, 0, &dummy, 0x0513, 100000000ull);
+        }
+    } else {
+        // Epilogue: warps 2..5 read TMEM lanes 32*(warp%4).. (= rows of this
+        // CTA's 128-row half), convert, and stage each column chunk as
+        // [column][row] in shared memory for one TMA store.
+        constexpr int CC = C::kChunkCols;
+        const float scale = C::kScaled ? __ldg(p.scale_a) * __ldg(p.scale_b) : 1.0f;
+        const uint32_t quarter = warp & 3u;
+        const int row_in_half = (int)(quarter * 32 + lane);
+        const bool issuer = warp == 2 && lane == 0;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        uint32_t chunk_seq = 0;
+        for (int t = cluster; t < num_tiles; t += nclusters) {
+            int mt, nt;
+            tile_coords(t, p.m_tiles, p.n_tiles, mt, nt);
+            if (!mbar_wait_sleepy(&sm.acc_full[acc], acc_phase, &sm.abort, 0x0521, true)) sm.epi_fail = 1;
+            named_sync(1, 128);
+            if (*(volatile int*)&sm.epi_fail) break;
+            tc_fence_after();
+            const int m0 = mt * 256 + (int)rank * 128;
+            const int m = m0 + row_in_half;
+            const int n_base = nt * 256;
+            const uint32_t t_addr = tmem + ((quarter * 32u) << 16) + (uint32_t)acc * 256u;
+            const uint32_t acc_empty_leader = mapa_shared(smem_u32(&sm.acc_empty[acc]), 0);
+#pragma unroll 1
+            for (int c = 0; c < C::kChunks; ++c) {
+                uint32_t r[CC];
+                tmem_ld_cols<CC>(t_addr + (uint32_t)(CC * c), r);
+                tmem_ld_wait();
+                if (c == C::kChunks - 1) {  // the accumulator is in registers: release it
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(acc_empty_leader);
+                }
+                if (p.tma_store) {
+                    uint8_t* stg = sm.out_stage[chunk_seq & 1u];
+                    if (issuer) bulk_wait_read<1>();  // the store that last used this buffer has read it
+                    named_sync(1, 128);
+                    if constexpr (C::kOutBytes == 2) {
+                        uint16_t* s16 = reinterpret_cast<uint16_t*>(stg);
+#pragma unroll
+                        for (int j = 0; j < CC; j += 2) {
+                            const float lo = __uint_as_float(r[j]) * scale, hi = __uint_as_float(r[j + 1]) * scale;
+                            const uint32_t v = C::kOut == Out::BF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
+                            s16[j * 128 + row_in_half] = (uint16_t)(v & 0xFFFFu);
+                            s16[(j + 1) * 128 + row_in_half] = (uint16_t)(v >> 16);
+                        }
+                    } else {
+                        uint32_t* s32 = reinterpret_cast<uint32_t*>(stg);
+#pragma unroll
+                        for (int j = 0; j < CC; ++j) s32[j * 128 + row_in_half] = r[j];
+                    }
+                    fence_proxy_async_smem();
+                    named_sync(1, 128);
+                    if (issuer && m0 < p.M && n_base + CC * c < p.N) {  // skip boxes wholly outside D
+                        tma_store_2d(&tmD, stg, m0, n_base + CC * c);
+                        bulk_commit();
+                    }
+                    ++chunk_seq;
+                } else if (m < p.M) {
+                    const size_t ldd = (size_t)p.M;
+#pragma unroll
+                    for (int j = 0; j < CC; j += 2) {
+                        const int n = n_base + CC * c + j;
+                        if constexpr (C::kOutBytes == 2) {
+                            uint16_t* drow = static_cast<uint16_t*>(p.D) + m;
+                            const float lo = __uint_as_float(r[j]) * scale, hi = __uint_as_float(r[j + 1]) * scale;
+                            const uint32_t v = C::kOut == Out::BF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
+                            if (n < p.N) drow[(size_t)n * ldd] = (uint16_t)(v & 0xFFFFu);
+                            if (n + 1 < p.N) drow[(size_t)(n + 1) * ldd] = (uint16_t)(v >> 16);
+                        } else {
+                            uint32_t* drow = static_cast<uint32_t*>(p.D) + m;
+                            if (n < p.N) drow[(size_t)n * ldd] = r[j];
+                            if (n + 1 < p.N) drow[(size_t)(n + 1) * ldd] = r[j + 1];
+                        }
+                    }
+                }
+            }
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+        if (issuer) bulk_wait<0>();  // every store of D has completed
+    }
+
+    tc_fence_before();
+    cluster_sync();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem, 512);
+    }
+}
+
+constexpr int kSmemBytes = (int)sizeof(Smem) + 1024;
+
+// 2-D tensor map over `rows` rows of `row_bytes` bytes (pitch `pitch`),
+// addressed in bytes, box 128 bytes x box_rows, 128-byte swizzle. Used for
+// every operand whatever its element type: TMA moves bytes, the MMA's
+// instruction descriptor gives them their type.
+static int encode_operand(CUtensorMap* map, const void* base, uint64_t row_bytes, uint64_t rows, uint32_t box_rows,
+                          CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
+    return encode_tmap_2d_u8(map, base, row_bytes, rows, row_bytes, 128, box_rows, swizzle);
+}
+
+template <class C>
+static int launch(const void* A, const void* B, void* D, int M, int N, int K, cudaStream_t stream,
+                  const float* scale_a = nullptr, const float* scale_b = nullptr) {
+    DeviceInfo d;
+    int st = require_sm100(&d);
+    if (st != GPLK_STATUS_OK) return st;
+    if (kSmemBytes > d.max_smem_optin) return GPLK_STATUS_UNSUPPORTED;
+    static thread_local uint64_t configured = 0;  // bit per device
+    static int capacity[64] = {0};                // clusters resident at once, per device
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return GPLK_STATUS_CUDA_ERROR;
+    if (!(configured & (1ull << dev))) {
+        if (cudaFuncSetAttribute(gemm_pair_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
+            cudaSuccess)
+            return GPLK_STATUS_LAUNCH_FAIL;
+        configured |= 1ull << dev;
+    }
+    if (capacity[dev] == 0) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)(d.sm_count & ~1), 1, 1);
+        cfg.blockDim = dim3(kThreads, 1, 1);
+        cfg.dynamicSmemBytes = (size_t)kSmemBytes;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = 2;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<C>, &cfg) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = d.sm_count / 2;
+        }
+        capacity[dev] = n;
+    }
+    CUtensorMap tmA, tmB, tmD;
+    if constexpr (C::kAKMajor) {
+        // A K-major (TN): M rows of K elements, boxes of 128 bytes (K) x 128 rows (M).
+        st = encode_operand(&tmA, A, (uint64_t)K * C::kInBytes, (uint64_t)M, 128);
+    } else {
+        // A column-major M x K: K rows of M elements, boxes of kRowElems (M) x kRowElems (K).
+        st = encode_operand(&tmA, A, (uint64_t)M * C::kInBytes, (uint64_t)K, (uint32_t)C::kRowElems,
+                            C::kA32BAtoms ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B);
+    }
+    if (st != GPLK_STATUS_OK) return st;
+    // B column-major K x N: N rows of K elements, boxes of 128 bytes (K) x 128 rows (N).
+    st = encode_operand(&tmB, B, (uint64_t)K * C::kInBytes, (uint64_t)N, 128);
+    if (st != GPLK_STATUS_OK) return st;
+    Params p;
+    memset(&p, 0, sizeof(p));
+    p.D = D;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.m_tiles = (M + 255) / 256;
+    p.n_tiles = (N + 255) / 256;
+    p.scale_a = scale_a;
+    p.scale_b = scale_b;
+    p.k_stages = (K + C::kRowElems * kSlabs - 1) / (C::kRowElems * kSlabs);
+    memset(&tmD, 0, sizeof(tmD));
+    p.tma_store = ((size_t)M * C::kOutBytes) % 16 == 0 && aligned16(D);
+    if (p.tma_store) {
+        st = C::kOutBytes == 2
+                 ? encode_tmap_2d_u16(&tmD, D, (uint64_t)M, (uint64_t)N, (uint64_t)M * 2, 128, C::kChunkCols)
+                 : encode_tmap_2d_u32(&tmD, D, (uint64_t)M, (uint64_t)N, (uint64_t)M * 4, 128, C::kChunkCols);
+        if (st != GPLK_STATUS_OK) return st;
+    }
+    const int tiles = p.m_tiles * p.n_tiles;
+    const int clusters = capacity[dev] < tiles ? capacity[dev] : tiles;
+    gemm_pair_kernel<C><<<2 * clusters, kThreads, kSmemBytes, stream>>>(tmA, tmB, tmD, p);
+    return launch_status(cudaGetLastError());
+}
+
+// Arguments shared by the four entry points. Operand pitches must be
+// multiples of 16 bytes for TMA: M and K multiples of 16 / element size.
+template <class C>
+static int checked_launch(const void* A, const void* B, void* D, int M, int N, int K, cudaStream_t stream) {
+    if (M < 0 || N < 0 || K < 0) return GPLK_STATUS_BAD_ARG;
+    if (M == 0 || N == 0) return GPLK_STATUS_OK;
+    constexpr int align = 16 / C::kInBytes;
+    if (K == 0 || M % align != 0 || K % align != 0) return GPLK_STATUS_BAD_ARG;
+    if (!A || !B || !D || !aligned16(A) || !aligned16(B)) return GPLK_STATUS_BAD_ARG;
+    return launch<C>(A, B, D, M, N, K, stream);
+}
+
+}  // namespace pair
+}  // namespace gplk
+
+extern "C" int gplk_gemm_bf16_nn(const uint16_t* A, const uint16_t* B, uint16_t* D, int M, int N, int K,
+                                 cudaStream_t stream) {
+    return gplk::pair::checked_launch<gplk::pair::CfgBF16>(A, B, D, M, N, K, stream);
+}
+
+extern "C" int gplk_gemm_f16_nn(const uint16_t* A, const uint16_t* B, uint16_t* D, int M, int N, int K,
+                                cudaStream_t stream) {
+    return gplk::pair::checked_launch<gplk::pair::CfgF16>(A, B, D, M, N, K, stream);
+}
+
+extern "C" int gplk_gemm_tf32_nn(const float* A, const float* B, float* D, int M, int N, int K,
+                                 cudaStream_t stream) {
+    return gplk::pair::checked_launch<gplk::pair::CfgTF32>(A, B, D, M, N, K, stream);
+}
+
+extern "C" int gplk_gemm_i8_nn(const int8_t* A, const int8_t* B, int32_t* D, int M, int N, int K,
+                               cudaStream_t stream) {
+    return gplk::pair::checked_launch<gplk::pair::CfgI8>(A, B, D, M, N, K, stream);
+}

@@ -16,9 +16,10 @@
 //   warps 2..5  epilogue: tcgen05.ld of the accumulator, scale, BF16, global
 //               stores. Warp w reads TMEM lanes 32*(w%4)..+31 (= tile rows).
 // FP8 double-buffers the accumulator (2 x 256 TMEM columns) so the epilogue of
-// one tile overlaps the main loop of the next. NVFP4 needs TMEM for per-stage
-// scale factors, so it keeps one accumulator and drains it into registers
-// before storing, releasing TMEM early.
+// one tile overlaps the main loop of the next. (FP8 problems with more than
+// 128 rows run on the CTA-pair kernel of gplk_gemm_pair.cu instead.) NVFP4
+// needs TMEM for per-stage scale factors, so it keeps one accumulator and
+// drains it into registers before storing, releasing TMEM early.
 // Every mbarrier wait is bounded; on timeout the kernel records
 // GPLK_STATUS_DEVICE_TIMEOUT, drains outstanding copies and MMAs, frees TMEM
 // and returns.
@@ -358,242 +359,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 
-// ------------------------------------------------------------ FP8, CTA pairs
-// A 2-CTA cluster computes a 256 x 256 tile with tcgen05.mma.cta_group::2
-// (M = 256, N = 256, K = 32): CTA r of the pair loads rows r*128..+127 of the
-// A tile and rows r*128..+127 of the B tile (N-major half) into its own
-// shared memory, so each SM streams 8 KiB of operands per 2.1 MFLOP
-// instruction instead of 12 KiB, and only the leader (rank 0) issues MMAs.
-// Both CTAs' TMA bytes land on the leader's `full` barrier; the leader's
-// MMA thread releases each stage in both CTAs with one commit per CTA, and
-// publishes each accumulator to both CTAs' epilogues the same way; the
-// leader's `acc_empty` collects the 8 epilogue warps of the pair.
-constexpr int kPairStages = 6;
-constexpr int kPairHalf = 128 * BK_BYTES;          // 16 KiB: 128 rows x 128 B
-constexpr int kPairStageBytes = 2 * kPairHalf;     // A half + B half
-constexpr int kPairGroupM = 16;
-
-constexpr int kOutChunkCols = 32;                   // columns of D per TMA store
-constexpr int kOutChunkBytes = 128 * kOutChunkCols * 2;  // 128 rows x 32 BF16 = 8 KiB
-
-struct __align__(1024) PairSmem {
-    uint8_t stage[kPairStages][kPairStageBytes];
-    uint8_t out_stage[2][kOutChunkBytes];  // epilogue staging for TMA stores of D
-    uint64_t full[kPairStages];
-    uint64_t empty[kPairStages];
-    uint64_t acc_full[2];
-    uint64_t acc_empty[2];
-    uint64_t drain;
-    uint32_t tmem_base;
-    int abort;
-    int epi_fail;
-};
-
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
-    gemm_pair_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                         const __grid_constant__ CUtensorMap tmD, const Params p) {
-    constexpr int S = kPairStages;
-    extern __shared__ uint8_t smem_raw[];
-    PairSmem& sm = *reinterpret_cast<PairSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    const uint32_t warp = warp_id_uniform();
-    const uint32_t lane = lane_id();
-    const uint32_t rank = cluster_ctarank();
-    const bool leader = rank == 0;
-    const int cluster = (int)(blockIdx.x >> 1);
-    const int nclusters = (int)(gridDim.x >> 1);
-    const int num_tiles = p.m_tiles * p.n_tiles;
-
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < S; ++i) {
-            mbar_init(&sm.full[i], 1);
-            mbar_init(&sm.empty[i], 1);
-        }
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&sm.acc_full[i], 1);
-            mbar_init(&sm.acc_empty[i], 8);
-        }
-        mbar_init(&sm.drain, 1);
-        sm.abort = 0;
-        sm.epi_fail = 0;
-        fence_barrier_init();
-    }
-    if (warp == 0 && lane == 0) {
-        tma_prefetch_desc(&tmA);
-        tma_prefetch_desc(&tmB);
-        if (p.tma_store) tma_prefetch_desc(&tmD);
-    }
-    if (warp == 1) {
-        tmem_alloc_pair(&sm.tmem_base, 512);
-        tmem_relinquish_pair();
-    }
-    tc_fence_before();
-    cluster_sync();
-    tc_fence_after();
-    const uint32_t tmem = sm.tmem_base;
-
-    if (warp == 0) {
-        if (lane == 0) {
-            int stage = 0;
-            uint32_t phase = 0;
-            uint32_t issued_mask = 0, issued_parity = 0;
-            bool ok = true;
-            for (int t = cluster; t < num_tiles && ok; t += nclusters) {
-                int mt, nt;
-                tile_coords(t, p.m_tiles, p.n_tiles, mt, nt, kPairGroupM);
-                for (int kb = 0; kb < p.k_stages; ++kb) {
-                    if (!mbar_wait_cluster(&sm.empty[stage], phase ^ 1u, &sm.abort, 0x0401)) {
-                        ok = false;
-                        break;
-                    }
-                    uint8_t* st = sm.stage[stage];
-                    const uint32_t full_leader = mapa_shared(smem_u32(&sm.full[stage]), 0);
-                    if (leader) mbar_arrive_expect_tx(&sm.full[stage], 2 * kPairStageBytes);
-                    tma_load_2d_pair(st, &tmA, full_leader, kb * BK_BYTES, mt * 256 + (int)rank * 128);
-                    tma_load_2d_pair(st + kPairHalf, &tmB, full_leader, kb * BK_BYTES, nt * 256 + (int)rank * 128);
-                    issued_mask |= 1u << stage;
-                    issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
-                    if (++stage == S) {
-                        stage = 0;
-                        phase ^= 1u;
-                    }
-                }
-            }
-            if (leader && (!ok || sm.abort)) {
-                // Drain: both CTAs' copies complete on the leader's barriers.
-                int dummy = 0;
-                for (int s2 = 0; s2 < S; ++s2)
-                    if (issued_mask & (1u << s2))
-                        mbar_wait_cluster(&sm.full[s2], (issued_parity >> s2) & 1u, &dummy, 0x0402, 100000000ull);
-            }
-        }
-    } else if (warp == 1) {
-        if (leader && lane == 0) {
-            const uint32_t idesc = idesc_e4m3_f32(256, 256);
-            int stage = 0;
-            uint32_t phase = 0;
-            int acc = 0;
-            uint32_t acc_phase = 0;
-            bool ok = true;
-            for (int t = cluster; t < num_tiles && ok; t += nclusters) {
-                if (!mbar_wait_cluster(&sm.acc_empty[acc], acc_phase ^ 1u, &sm.abort, 0x0411)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t d_tmem = tmem + (uint32_t)acc * 256u;
-                for (int kb = 0; kb < p.k_stages; ++kb) {
-                    if (!mbar_wait_cluster(&sm.full[stage], phase, &sm.abort, 0x0412)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t a_addr = smem_u32(sm.stage[stage]);
-                    const uint32_t b_addr = a_addr + kPairHalf;
-#pragma unroll
-                    for (int j = 0; j < 4; ++j)
-                        mma_pair_f8f6f4(d_tmem, desc_kmajor_sw128(a_addr + 32 * j), desc_kmajor_sw128(b_addr + 32 * j),
-                                        idesc, (kb | j) != 0);
-                    const uint32_t e = smem_u32(&sm.empty[stage]);
-                    tc_commit_pair(mapa_shared(e, 0));
-                    tc_commit_pair(mapa_shared(e, 1));
-                    if (++stage == S) {
-                        stage = 0;
-                        phase ^= 1u;
-                    }
-                }
-                if (!ok) break;
-                const uint32_t f = smem_u32(&sm.acc_full[acc]);
-                tc_commit_pair(mapa_shared(f, 0));
-                tc_commit_pair(mapa_shared(f, 1));
-                if (++acc == 2) {
-                    acc = 0;
-                    acc_phase ^= 1u;
-                }
-            }
-            tc_commit_pair(mapa_shared(smem_u32(&sm.drain), 0));
-            int dummy = 0;
-            mbar_wait_cluster(&sm.drain, 0, &dummy, 0x0413, 100000000ull);
-        }
-    } else {
-        // Epilogue: warps 2..5 read TMEM lanes 32*(warp%4).. (= rows of this
-        // CTA's half). With TMA stores, each 32-column chunk is staged as
-        // [column][row] BF16 in shared memory (double-buffered) and written
-        // by one bulk tensor store; the TMA unit clips partial tiles.
-        const uint32_t quarter = warp & 3u;
-        const int row_in_half = (int)(quarter * 32 + lane);
-        const float scale = __ldg(p.scale_a) * __ldg(p.scale_b);
-        const bool issuer = warp == 2 && lane == 0;
-        int acc = 0;
-        uint32_t acc_phase = 0;
-        uint32_t chunk_seq = 0;
-        for (int t = cluster; t < num_tiles; t += nclusters) {
-            int mt, nt;
-            tile_coords(t, p.m_tiles, p.n_tiles, mt, nt, kPairGroupM);
-            // All four epilogue warps leave together if any of them gave up.
-            if (!mbar_wait_sleepy(&sm.acc_full[acc], acc_phase, &sm.abort, 0x0421, true)) sm.epi_fail = 1;
-            named_sync(1, 128);
-            if (*(volatile int*)&sm.epi_fail) break;
-            tc_fence_after();
-            const int m0 = mt * 256 + (int)rank * 128;
-            const int m = m0 + row_in_half;
-            const int n_base = nt * 256;
-            const uint32_t t_addr = tmem + ((quarter * 32u) << 16) + (uint32_t)acc * 256u;
-            const uint32_t acc_empty_leader = mapa_shared(smem_u32(&sm.acc_empty[acc]), 0);
-#pragma unroll 1
-            for (int c = 0; c < 8; ++c) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(t_addr + 32u * c, r);
-                tmem_ld_wait();
-                if (c == 7) {  // the accumulator is in registers: release it to the MMA
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive_cluster(acc_empty_leader);
-                }
-                if (p.tma_store) {
-                    uint16_t* stg = reinterpret_cast<uint16_t*>(sm.out_stage[chunk_seq & 1u]);
-                    if (issuer) bulk_wait_read<1>();  // the store that last used this buffer has read it
-                    named_sync(1, 128);
-#pragma unroll
-                    for (int j = 0; j < 32; j += 2) {
-                        const uint32_t v = pack_bf16x2(__uint_as_float(r[j]) * scale, __uint_as_float(r[j + 1]) * scale);
-                        stg[j * 128 + row_in_half] = (uint16_t)(v & 0xFFFFu);
-                        stg[(j + 1) * 128 + row_in_half] = (uint16_t)(v >> 16);
-                    }
-                    fence_proxy_async_smem();
-                    named_sync(1, 128);
-                    if (issuer && m0 < p.M && n_base + kOutChunkCols * c < p.N) {  // skip boxes wholly outside D
-                        tma_store_2d(&tmD, stg, m0, n_base + kOutChunkCols * c);
-                        bulk_commit();
-                    }
-                    ++chunk_seq;
-                } else if (m < p.M) {
-                    uint16_t* drow = p.D + m;
-                    const size_t ldd = (size_t)p.M;
-#pragma unroll
-                    for (int j = 0; j < 32; j += 2) {
-                        const uint32_t v = pack_bf16x2(__uint_as_float(r[j]) * scale, __uint_as_float(r[j + 1]) * scale);
-                        const int n = n_base + 32 * c + j;
-                        if (n < p.N) drow[(size_t)n * ldd] = (uint16_t)(v & 0xFFFFu);
-                        if (n + 1 < p.N) drow[(size_t)(n + 1) * ldd] = (uint16_t)(v >> 16);
-                    }
-                }
-            }
-            if (++acc == 2) {
-                acc = 0;
-                acc_phase ^= 1u;
-            }
-        }
-        if (issuer) bulk_wait<0>();  // every store of D has completed
-    }
-
-    tc_fence_before();
-    cluster_sync();
-    if (warp == 1) {
-        tc_fence_after();
-        tmem_dealloc_pair(tmem, 512);
-    }
-}
-
 template <bool NVF4>
 static int smem_bytes() {
     return (int)sizeof(Smem<NVF4>) + 1024;
@@ -656,81 +421,6 @@ static int launch(const uint8_t* A, const uint8_t* B, const uint8_t* SFA, const 
     return launch_status(cudaGetLastError());
 }
 
-// Clusters of two that can be resident at once (one CTA per SM): the
-// persistent pair grid is twice this, capped by the tile count.
-static int pair_cluster_capacity(const DeviceInfo& d, int smem) {
-    static int cached[64] = {0};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64) return d.sm_count / 2;
-    if (cached[dev] == 0) {
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((unsigned)(d.sm_count & ~1), 1, 1);
-        cfg.blockDim = dim3(kThreads, 1, 1);
-        cfg.dynamicSmemBytes = (size_t)smem;
-        cudaLaunchAttribute attr;
-        attr.id = cudaLaunchAttributeClusterDimension;
-        attr.val.clusterDim.x = 2;
-        attr.val.clusterDim.y = 1;
-        attr.val.clusterDim.z = 1;
-        cfg.attrs = &attr;
-        cfg.numAttrs = 1;
-        int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, gemm_pair_fp8_kernel, &cfg) != cudaSuccess || n <= 0) {
-            cudaGetLastError();
-            n = d.sm_count / 2;
-        }
-        cached[dev] = n;
-    }
-    return cached[dev];
-}
-
-static int launch_pair_fp8(const uint8_t* A, const uint8_t* B, uint16_t* D, int M, int N, int K, const float* sa,
-                           const float* sb, cudaStream_t stream) {
-    DeviceInfo d;
-    int st = require_sm100(&d);
-    if (st != GPLK_STATUS_OK) return st;
-    const int smem = (int)sizeof(PairSmem) + 1024;
-    if (smem > d.max_smem_optin) return GPLK_STATUS_UNSUPPORTED;
-    static thread_local uint64_t configured = 0;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!(configured & (1ull << dev))) {
-        if (cudaFuncSetAttribute(gemm_pair_fp8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-            cudaSuccess)
-            return GPLK_STATUS_LAUNCH_FAIL;
-        configured |= 1ull << dev;
-    }
-    CUtensorMap tmA, tmB;
-    st = encode_tmap_2d_u8(&tmA, A, (uint64_t)K, (uint64_t)M, (uint64_t)K, BK_BYTES, 128);
-    if (st != GPLK_STATUS_OK) return st;
-    st = encode_tmap_2d_u8(&tmB, B, (uint64_t)K, (uint64_t)N, (uint64_t)K, BK_BYTES, 128);
-    if (st != GPLK_STATUS_OK) return st;
-    Params p;
-    memset(&p, 0, sizeof(p));
-    p.D = D;
-    p.scale_a = sa;
-    p.scale_b = sb;
-    p.M = M;
-    p.N = N;
-    p.K = K;
-    p.m_tiles = (M + 255) / 256;
-    p.n_tiles = (N + 255) / 256;
-    p.k_stages = (K + BK_BYTES - 1) / BK_BYTES;
-    CUtensorMap tmD;
-    memset(&tmD, 0, sizeof(tmD));
-    p.tma_store = (M % 8 == 0) && aligned16(D);
-    if (p.tma_store) {
-        st = encode_tmap_2d_u16(&tmD, D, (uint64_t)M, (uint64_t)N, (uint64_t)M * 2, 128, kOutChunkCols);
-        if (st != GPLK_STATUS_OK) return st;
-    }
-    const int tiles = p.m_tiles * p.n_tiles;
-    int clusters = pair_cluster_capacity(d, smem);
-    if (clusters > tiles) clusters = tiles;
-    gemm_pair_fp8_kernel<<<2 * clusters, kThreads, smem, stream>>>(tmA, tmB, tmD, p);
-    return launch_status(cudaGetLastError());
-}
-
 }  // namespace gemm_tc
 }  // namespace gplk
 
@@ -743,8 +433,9 @@ extern "C" int gplk_gemm_fp8_tn(const uint8_t* A, const uint8_t* B, uint16_t* D,
     if (!A || !B || !D || !scale_a || !scale_b) return GPLK_STATUS_BAD_ARG;
     if (!aligned16(A) || !aligned16(B)) return GPLK_STATUS_BAD_ARG;
     // Problems with at least two 128-row blocks run on CTA pairs (256 x 256
-    // tiles, cta_group::2); a single row block runs on single CTAs.
-    if (M > 128) return gemm_tc::launch_pair_fp8(A, B, D, M, N, K, scale_a, scale_b, stream);
+    // tiles, cta_group::2, gplk_gemm_pair.cu); a single row block runs on
+    // single CTAs (128 x 256 tiles).
+    if (M > 128) return pair::launch<pair::CfgFP8>(A, B, D, M, N, K, stream, scale_a, scale_b);
     return gemm_tc::launch<false>(A, B, nullptr, nullptr, D, M, N, K, scale_a, scale_b, stream);
 }
 

@@ -3,6 +3,7 @@
 #include "gplk_core.cu"
 #include "gplk_memstream.cu"
 #include "gplk_sgemm.cu"
+#include "gplk_gemm_pair.cu"
 #include "gplk_gemm_tc.cu"
 #include "gplk_powervirus.cu"
 #include "gplk_powervirus_noalloc.cu"

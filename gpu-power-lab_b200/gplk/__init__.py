@@ -88,6 +88,9 @@ def lib() -> ctypes.CDLL:
     L.gplk_gemm_fp8_tn.argtypes = [_p, _p, _p, _i, _i, _i, _p, _p, _p]
     L.gplk_gemm_nvfp4_tn.restype = _i
     L.gplk_gemm_nvfp4_tn.argtypes = [_p, _p, _p, _p, _p, _i, _i, _i, _p, _p]
+    for name in ("gplk_gemm_bf16_nn", "gplk_gemm_f16_nn", "gplk_gemm_tf32_nn", "gplk_gemm_i8_nn"):
+        getattr(L, name).restype = _i
+        getattr(L, name).argtypes = [_p, _p, _p, _i, _i, _i, _p]
     L.gplk_selftest_wait_timeout.restype = _i
     L.gplk_selftest_wait_timeout.argtypes = [ctypes.c_ulonglong, _p, _p]
     L.gplk_nvfp4_sf_bytes.restype = _sz
@@ -183,6 +186,21 @@ def gemm_nvfp4_tn(A, B, SFA, SFB, D, K: int, alpha, stream=None) -> None:
     assert A.shape[1] * 2 == K and B.shape[1] * 2 == K and D.numel() == M * N
     _check("gplk_gemm_nvfp4_tn", lib().gplk_gemm_nvfp4_tn(_ptr(A), _ptr(B), _ptr(SFA), _ptr(SFB), _ptr(D),
                                                             M, N, K, _ptr(alpha), _stream(stream)))
+
+
+# ------------------------------------------------------------ dense tensor-core GEMMs
+
+_NN = {"bf16": "gplk_gemm_bf16_nn", "f16": "gplk_gemm_f16_nn", "tf32": "gplk_gemm_tf32_nn", "i8": "gplk_gemm_i8_nn"}
+
+
+def gemm_nn(prec: str, A, B, D, M: int, N: int, K: int, stream=None) -> None:
+    """Column-major D = A @ B (cublasGemmEx NN layout). A holds M x K with
+    M contiguous, B holds K x N with K contiguous, D holds M x N with M
+    contiguous: as torch tensors, A is (K, M), B is (N, K) and D is (N, M),
+    all contiguous. prec: bf16 | f16 | tf32 | i8."""
+    assert A.numel() == M * K and B.numel() == K * N and D.numel() == M * N
+    fn = _NN[prec]
+    _check(fn, getattr(lib(), fn)(_ptr(A), _ptr(B), _ptr(D), M, N, K, _stream(stream)))
 
 
 # ------------------------------------------------------------ powervirus

@@ -7,9 +7,13 @@
  *                runner/src/workload_gemm.c:155-163
  *   fp8, fp4     gpl_lt_* from libgplk (tcgen05 E4M3 / NVFP4 GEMMs), which
  *                the reference rejected on this op (:84-89)
- *   tf32, fp16, bf16, fp64, int8
- *                cublasGemmEx with the reference's type mapping (:45-79):
- *                plain library GEMMs, unchanged
+ *   bf16, fp16, tf32, int8
+ *                gplk_gemm_{bf16,f16,tf32,i8}_nn: tcgen05 GEMMs on CTA pairs in
+ *                the same column-major NN layout and output types as the
+ *                reference's cublasGemmEx call (:45-79, :155-163).
+ *                GPL_GEMM_BACKEND=cublas keeps these on cublasGemmEx.
+ *   fp64         cublasGemmEx with the reference's type mapping: a plain
+ *                library GEMM (tcgen05 has no FP64 kind)
  *
  * Square N x N x N problems, one C per stream, warm-up and steady phases by
  * wall clock, a device sync every 8 x streams launches (:167-219).
@@ -34,12 +38,35 @@ typedef struct {
     const void *alpha, *beta;
 } gemm_cublas_t;
 
-typedef enum { PATH_GPLK_SGEMM, PATH_GPLK_LT, PATH_CUBLAS } gemm_path_t;
+typedef enum { PATH_GPLK_SGEMM, PATH_GPLK_LT, PATH_GPLK_TC, PATH_CUBLAS } gemm_path_t;
 
 static gemm_path_t path_for(gpl_prec_t p) {
     if (p == GPL_PREC_FP32) return PATH_GPLK_SGEMM;
     if (p == GPL_PREC_FP8 || p == GPL_PREC_FP4) return PATH_GPLK_LT;
-    return PATH_CUBLAS;
+    if (p == GPL_PREC_FP64) return PATH_CUBLAS;
+    const char *b = getenv("GPL_GEMM_BACKEND");
+    if (b && !strcmp(b, "cublas")) return PATH_CUBLAS;
+    return PATH_GPLK_TC;
+}
+
+#define TC_SIZE_MSG                                                                      \
+    "size unsupported by the tcgen05 GEMM (a multiple of 8 for bf16/fp16, 4 for tf32, 16 " \
+    "for int8 is required); GPL_GEMM_BACKEND=cublas runs it on cublasGemmEx"
+
+/* One tcgen05 GEMM of the rung's precision: column-major C = A * B. */
+static int gplk_tc_gemm(gpl_prec_t p, const void *A, const void *B, void *C, int n, cudaStream_t s) {
+    switch (p) {
+        case GPL_PREC_BF16:
+            return gplk_gemm_bf16_nn((const uint16_t *)A, (const uint16_t *)B, (uint16_t *)C, n, n, n, s);
+        case GPL_PREC_FP16:
+            return gplk_gemm_f16_nn((const uint16_t *)A, (const uint16_t *)B, (uint16_t *)C, n, n, n, s);
+        case GPL_PREC_TF32:
+            return gplk_gemm_tf32_nn((const float *)A, (const float *)B, (float *)C, n, n, n, s);
+        case GPL_PREC_INT8:
+            return gplk_gemm_i8_nn((const int8_t *)A, (const int8_t *)B, (int32_t *)C, n, n, n, s);
+        default:
+            return GPLK_STATUS_BAD_ARG;
+    }
 }
 
 /* cublasGemmEx types for the precisions that stay on the library. */
@@ -126,7 +153,7 @@ int gpl_workload_gemm_run(gpl_workload_ctx_t *ctx) {
         }
     } else {
         size_t in_b = 4, out_b = 4;
-        if (path == PATH_CUBLAS) cublas_types(a->precision, &cb[0], &in_b, &out_b);
+        if (path != PATH_GPLK_SGEMM) cublas_types(a->precision, &cb[0], &in_b, &out_b);
         G_CUDA(cudaMalloc(&dA, nn * in_b));
         G_CUDA(cudaMalloc(&dB, nn * in_b));
         G_CUDA(cudaMemset(dA, 0x3c, nn * in_b));
@@ -161,6 +188,9 @@ int gpl_workload_gemm_run(gpl_workload_ctx_t *ctx) {
         } else if (path == PATH_GPLK_LT) {                                                              \
             _r = gpl_lt_enqueue(&lt[i], 1);                                                             \
             if (_r) ctx->error = "gemm_lt enqueue failed";                                              \
+        } else if (path == PATH_GPLK_TC) {                                                              \
+            _r = gplk_tc_gemm(a->precision, dA, dB, dC[i], N, st[i]);                                   \
+            if (_r) ctx->error = _r == GPLK_STATUS_BAD_ARG ? TC_SIZE_MSG : gplk_status_string(_r);      \
         } else {                                                                                        \
             _r = cublasGemmEx(cb[i].h, CUBLAS_OP_N, CUBLAS_OP_N, N, N, N, cb[i].alpha, dA, cb[i].in_t,  \
                               N, dB, cb[i].in_t, N, cb[i].beta, dC[i], cb[i].out_t, N, cb[i].comp_t,   \

@@ -114,6 +114,29 @@ int gplk_gemm_nvfp4_tn(const uint8_t *A, const uint8_t *B, const uint8_t *SFA,
  * a K extent of k elements. */
 size_t gplk_nvfp4_sf_bytes(int rows, int k);
 
+/* ------------------------------------------------------------ dense tensor-core GEMMs
+ * C = A * B in the reference's cublasGemmEx layout: every matrix column-major,
+ * no transposes, alpha = 1, beta = 0:
+ *   A: M x K (ld = M), B: K x N (ld = K), D: M x N (ld = M).
+ * Replaces cublasGemmEx(CUBLAS_OP_N, CUBLAS_OP_N, ...) at
+ * runner/src/workload_gemm.c:155-163, :174-179, :199-204 for the precisions
+ * that file maps at :44-79:
+ *   bf16  BF16 in, FP32 accumulate, BF16 out   (CUDA_R_16BF, CUBLAS_COMPUTE_32F)
+ *   f16   FP16 in, FP32 accumulate, FP16 out   (CUDA_R_16F, CUBLAS_COMPUTE_16F:
+ *         the reference allows FP16 accumulation; this accumulates in FP32)
+ *   tf32  FP32 in, TF32 products, FP32 out      (CUBLAS_COMPUTE_32F_FAST_TF32)
+ *   i8    S8 in, S32 accumulate, S32 out        (CUDA_R_8I, CUBLAS_COMPUTE_32I)
+ * Requires M and K multiples of 16 / element size (8 for bf16/f16, 4 for
+ * tf32, 16 for i8) and 16-byte aligned A and B; N is free. */
+int gplk_gemm_bf16_nn(const uint16_t *A, const uint16_t *B, uint16_t *D, int M, int N, int K,
+                      cudaStream_t stream);
+int gplk_gemm_f16_nn(const uint16_t *A, const uint16_t *B, uint16_t *D, int M, int N, int K,
+                     cudaStream_t stream);
+int gplk_gemm_tf32_nn(const float *A, const float *B, float *D, int M, int N, int K,
+                      cudaStream_t stream);
+int gplk_gemm_i8_nn(const int8_t *A, const int8_t *B, int32_t *D, int M, int N, int K,
+                    cudaStream_t stream);
+
 /* ------------------------------------------------------------ powervirus */
 
 #define GPLK_PV_ROLE_TENSOR 0  /* tcgen05 FP8 MMA into TMEM on smem-resident tiles */

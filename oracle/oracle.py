@@ -56,6 +56,8 @@ def lib() -> ctypes.CDLL:
         L.gplo_max_threads.restype = _i
         L.gplo_sgemm_f64acc.argtypes = [_p, _p, _p, _i, _i, _i, _i, _i, _i, _i]
         L.gplo_sgemm_f32_naive.argtypes = [_p, _p, _p, _i, _i, _i, _i]
+        L.gplo_gemm_nn_f64.argtypes = [_p, _p, _p, _i, _i, _i, _i]
+        L.gplo_gemm_nn_i8.argtypes = [_p, _p, _p, _i, _i, _i, _i]
         L.gplo_e4m3_decode.restype = _f
         L.gplo_e4m3_decode.argtypes = [ctypes.c_uint8]
         L.gplo_e4m3_encode.restype = ctypes.c_uint8
@@ -146,6 +148,33 @@ def sgemm_f32_naive(A: np.ndarray, B: np.ndarray, threads: int = 0) -> np.ndarra
     C = np.empty((M, N), dtype=np.float32)
     lib().gplo_sgemm_f32_naive(_ptr(A), _ptr(B), _ptr(C), M, N, K, threads)
     return C
+
+
+def gemm_nn_f64(A: np.ndarray, B: np.ndarray, M: int, N: int, K: int, threads: int = 0) -> np.ndarray:
+    """Column-major C = A * B (cublasGemmEx OP_N/OP_N). A: float32 values of
+    the M x K matrix stored column-major (numpy shape (K, M)), B: K x N
+    column-major (shape (N, K)). Returns C as float64 of shape (N, M)."""
+    A = np.ascontiguousarray(A, dtype=np.float32)
+    B = np.ascontiguousarray(B, dtype=np.float32)
+    assert A.size == M * K and B.size == K * N
+    C = np.empty((N, M), dtype=np.float64)
+    lib().gplo_gemm_nn_f64(_ptr(A), _ptr(B), _ptr(C), M, N, K, threads)
+    return C
+
+
+def gemm_nn_i8(A: np.ndarray, B: np.ndarray, M: int, N: int, K: int, threads: int = 0) -> np.ndarray:
+    """The same product of S8 matrices, exact, as int32 of shape (N, M)."""
+    A = np.ascontiguousarray(A, dtype=np.int8)
+    B = np.ascontiguousarray(B, dtype=np.int8)
+    assert A.size == M * K and B.size == K * N
+    C = np.empty((N, M), dtype=np.int32)
+    lib().gplo_gemm_nn_i8(_ptr(A), _ptr(B), _ptr(C), M, N, K, threads)
+    return C
+
+
+def f16_round(x: np.ndarray) -> np.ndarray:
+    """Round float32 -> IEEE binary16 (RNE) -> float32."""
+    return np.asarray(x, dtype=np.float32).astype(np.float16).astype(np.float32)
 
 
 # ------------------------------------------------------------ narrow formats
@@ -297,6 +326,8 @@ def ref_lib() -> ctypes.CDLL:
         L.ref_lt_new.restype = _p
         L.ref_lt_delete.argtypes = [_p]
         L.ref_lt_ptrs.argtypes = [_p, _p]
+        L.ref_gemm_ex.restype = _i
+        L.ref_gemm_ex.argtypes = [_i, _p, _p, _p, _i, _p]
         _ref = L
     return _ref
 

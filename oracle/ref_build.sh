@@ -7,6 +7,7 @@
 #   args.c            gpl_args_defaults / gpl_prec_name
 #   util.c            logging helpers
 #   ref_shim.cu       includes workload_memstream.cu and workload_powervirus.cu
+#   ref_gemm_shim.c   includes workload_gemm.c (the cublasGemmEx GEMM rung)
 # Usage: oracle/ref_build.sh [REFERENCE_ROOT]   (default /root/reference)
 set -euo pipefail
 REF=${1:-/root/reference}
@@ -26,5 +27,6 @@ gcc -std=gnu11 -O2 -fPIC -I"$SRC" -I/usr/local/cuda/include -c "$SRC/util.c" -o 
 gcc -std=gnu11 -O2 -fPIC -I"$SRC" -I/usr/local/cuda/include -c "$SRC/workload_util.c" -o "$TMP/workload_util.o"
 nvcc $GEN -O2 -Xcompiler -fPIC -I"$SRC" -c "$SRC/gemm_lt.cu" -o "$TMP/gemm_lt.o"
 nvcc $GEN -O2 -Xcompiler -fPIC -I"$SRC" -c "$HERE/ref_shim.cu" -o "$TMP/ref_shim.o"
+gcc -std=gnu11 -O2 -fPIC -I"$SRC" -I/usr/local/cuda/include -c "$HERE/ref_gemm_shim.c" -o "$TMP/ref_gemm_shim.o"
 nvcc $GEN -shared -o "$OUT/libgpl_ref.so" "$TMP"/*.o -lcublasLt -lcublas
 echo "ref_build: wrote $OUT/libgpl_ref.so"

@@ -38,4 +38,5 @@ if [ -x "$R" ]; then
   rung ref_sgemm_fp32 "$R" --op sgemm --precision fp32 --size 1024
   rung ref_sgemm_fp4_rejected "$R" --op sgemm --precision fp4 --size 4096
   rung ref_powervirus "$R" --op powervirus --size 4096 --duty-on-ms 100 --duty-off-ms 100
+  rung ref_powervirus_capped "$R" --op powervirus --size 8192 --tensor-backend cublas --precision bf16 --mix-fma 0 --mix-dram 0
 fi

@@ -12,6 +12,10 @@ prints one JSON object (not collected by pytest; run on a GPU):
              vs gplk_gemm_fp8_tn, 8192^3
   nvfp4      cuBLASLt NVFP4 with VEC16_UE4M3 scales (oracle/lt_nvfp4.cu)
              vs gplk_gemm_nvfp4_tn, 2048..16384
+  nn         the reference's cublasGemmEx GEMM rung compiled from
+             runner/src/workload_gemm.c (oracle/ref_gemm_shim.c) vs
+             gplk_gemm_{bf16,f16,tf32,i8}_nn, 8192^3, identical operands:
+             random values and the rung's own 0x3c byte fill
 """
 from __future__ import annotations
 
@@ -213,8 +217,51 @@ def nvfp4(out):
     out["nvfp4_TFLOPs"] = res
 
 
+def nn(out):
+    n = 8192
+    L = oracle.ref_lib()
+    prec_code = {"tf32": 2, "f16": 3, "bf16": 4, "i8": 7}  # gpl_prec_t (runner/src/args.h:30-39)
+    tf = lambda ms: 2 * n ** 3 / (ms / 1e3) / 1e12
+    st = lambda: ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    res = {}
+    for prec in ("bf16", "f16", "tf32", "i8"):
+        r = {}
+        for label in ("random", "fill_0x3c"):
+            if prec == "i8":
+                A = torch.randint(-128, 128, (n, n), dtype=torch.int8, device="cuda")
+                B = torch.randint(-128, 128, (n, n), dtype=torch.int8, device="cuda")
+                D = torch.empty(n, n, dtype=torch.int32, device="cuda")
+            else:
+                dt = {"bf16": torch.bfloat16, "f16": torch.float16, "tf32": torch.float32}[prec]
+                A = (torch.rand(n, n, device="cuda") * 2 - 1).to(dt)
+                B = (torch.rand(n, n, device="cuda") * 2 - 1).to(dt)
+                D = torch.empty(n, n, dtype=dt, device="cuda")
+            if label == "fill_0x3c":
+                A.view(torch.uint8).fill_(0x3C)
+                B.view(torch.uint8).fill_(0x3C)
+            Dr = torch.empty_like(D)
+            torch.cuda.synchronize()
+            rc = L.ref_gemm_ex(prec_code[prec], A.data_ptr(), B.data_ptr(), Dr.data_ptr(), n, st())
+            torch.cuda.synchronize()
+            case = {}
+            for name, fn in (("reference_cublasGemmEx", lambda: L.ref_gemm_ex(prec_code[prec], A.data_ptr(),
+                                                                               B.data_ptr(), Dr.data_ptr(), n,
+                                                                               st())),
+                             (f"gplk_gemm_{prec}_nn", lambda: gplk.gemm_nn(prec, A, B, D, n, n, n))):
+                if name.startswith("reference") and rc != 0:
+                    case[name] = f"cublas status {rc}"
+                    continue
+                ms, mhz, w = sustained(fn)
+                case[name] = {"tflops": round(tf(ms), 1), "sm_mhz": mhz, "watts": w}
+            r[label] = case
+            del A, B, D, Dr
+            torch.cuda.empty_cache()
+        res[prec] = r
+    out["nn_8192_TFLOPs"] = res
+
+
 if __name__ == "__main__":
-    which = sys.argv[1:] or ["memstream", "sgemm", "fp8", "nvfp4"]
+    which = sys.argv[1:] or ["memstream", "sgemm", "fp8", "nvfp4", "nn"]
     out = {"device": torch.cuda.get_device_name()}
     for w in which:
         globals()[w](out)

@@ -60,7 +60,9 @@ def test_memstream_rung(tmp_path):
 
 @needs_runner
 @pytest.mark.parametrize("prec,size,min_tflops", [("fp32", 1024, 10.0), ("fp8", 8192, 1000.0),
-                                                  ("fp4", 8192, 1000.0), ("bf16", 8192, 500.0)])
+                                                  ("fp4", 8192, 1000.0), ("bf16", 8192, 500.0),
+                                                  ("fp16", 8192, 500.0), ("tf32", 8192, 250.0),
+                                                  ("int8", 8192, 1000.0), ("fp64", 2048, 1.0)])
 def test_gemm_ladder_rungs(prec, size, min_tflops, tmp_path):
     res, s, _ = run_rung(GPLK_RUNNER, tmp_path, "--op", "sgemm", "--precision", prec, "--size", str(size))
     _ok(res, s)
@@ -174,3 +176,20 @@ def test_powervirus_summary_extended_contract_and_violation_units(tmp_path):
     _ok(res, s)
     S.validate_doc(s)
     assert s["transient"]["power_violation_us"] <= s["timing"]["steady_ms"] * 1e3 * 1.05
+
+
+@needs_runner
+def test_gemm_backend_switch_keeps_cublas(tmp_path):
+    """GPL_GEMM_BACKEND=cublas runs the bf16 rung on cublasGemmEx, as the
+    reference does; the default runs it on the tcgen05 kernel."""
+    res, s, _ = run_rung(GPLK_RUNNER, tmp_path, "--op", "sgemm", "--precision", "bf16", "--size", "4096",
+                         env={"GPL_GEMM_BACKEND": "cublas"})
+    _ok(res, s)
+    assert s["compute"]["tflops_measured"] > 300.0
+
+
+@needs_runner
+def test_tc_gemm_rejects_unaligned_size_with_hint(tmp_path):
+    res, s, _ = run_rung(GPLK_RUNNER, tmp_path, "--op", "sgemm", "--precision", "int8", "--size", "1000")
+    assert res.returncode == 5
+    assert s["result"] == "cuda_error" and "GPL_GEMM_BACKEND=cublas" in s.get("error_message", "")

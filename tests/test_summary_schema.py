@@ -262,3 +262,15 @@ def test_runner_output_meets_extended_contract(path):
     else:
         with pytest.raises(ValueError):
             S.to_v1(doc)
+
+
+def test_violation_time_units_in_captured_summaries():
+    """The reference emitter reports NVML's nanosecond violation counter as
+    microseconds: its capped powervirus capture claims more power-cap time
+    than the steady window lasted. The drop-in emitter's never does."""
+    ref = json.loads((GOLDEN / "ref_powervirus_capped.json").read_text())
+    assert ref["transient"]["power_violation_us"] / 1e6 > 100 * ref["timing"]["steady_ms"] / 1e3
+    assert ref["transient"]["power_violation_us"] / 1e9 <= 1.05 * ref["timing"]["steady_ms"] / 1e3  # as ns it fits
+    for p in GOLDEN.glob("gplk_*.json"):
+        d = json.loads(p.read_text())
+        assert d["transient"]["power_violation_us"] / 1e6 <= 1.05 * d["timing"]["steady_ms"] / 1e3, p.name
