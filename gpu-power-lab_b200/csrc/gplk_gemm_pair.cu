@@ -48,7 +48,13 @@ constexpr int kSlabs = 2;                 // K slabs per stage (8 MMAs)
 constexpr int kStages = 3;
 constexpr int kOperandBytes = kSlabs * kSlab;    // A (or B) part of a stage: 32 KiB
 constexpr int kStageBytes = 2 * kOperandBytes;   // 64 KiB per CTA
-constexpr int kGroupM = 16;               // raster group along M (pair tiles)
+constexpr int kMaxGroupM = 16;            // raster group along M (pair tiles), upper bound
+#ifndef GPLK_PAIR_PANEL_BUDGET
+#define GPLK_PAIR_PANEL_BUDGET (32u << 20)
+#endif
+// Bytes of A row panels a raster group may keep live in L2: a group of g
+// pair-tiles along M shares g panels of 256 rows x K of A while it walks N.
+constexpr size_t kPanelBudget = GPLK_PAIR_PANEL_BUDGET;
 constexpr int kOutChunkBytes = 8192;      // epilogue staging: 8 KiB column chunks
 
 // Operand kind, A/B element format code in the instruction descriptor,
@@ -139,6 +145,7 @@ struct Params {
     const float* scale_b;
     int M, N, K;  // K in elements
     int m_tiles, n_tiles, k_stages;
+    int group_m;    // raster group along M (pair tiles)
     int tma_store;  // stage the epilogue through shared memory and TMA-store it
 };
 
@@ -155,11 +162,11 @@ struct __align__(1024) Smem {
     int epi_fail;
 };
 
-__device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int& mt, int& nt) {
-    const int per_group = kGroupM * n_tiles;
+__device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int group_m, int& mt, int& nt) {
+    const int per_group = group_m * n_tiles;
     const int group = t / per_group;
-    const int first_m = group * kGroupM;
-    const int gsize = min(m_tiles - first_m, kGroupM);
+    const int first_m = group * group_m;
+    const int gsize = min(m_tiles - first_m, group_m);
     const int r = t % per_group;
     mt = first_m + r % gsize;
     nt = r / gsize;
@@ -228,7 +235,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             bool ok = true;
             for (int t = cluster; t < num_tiles && ok; t += nclusters) {
                 int mt, nt;
-                tile_coords(t, p.m_tiles, p.n_tiles, mt, nt);
+                tile_coords(t, p.m_tiles, p.n_tiles, p.group_m, mt, nt);
                 const int m_base = mt * 256 + (int)rank * 128;
                 for (int kb = 0; kb < p.k_stages; ++kb) {
                     if (!mbar_wait_cluster(&sm.empty[stage], phase ^ 1u, &sm.abort, 0x0501)) {
@@ -336,7 +343,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         uint32_t chunk_seq = 0;
         for (int t = cluster; t < num_tiles; t += nclusters) {
             int mt, nt;
-            tile_coords(t, p.m_tiles, p.n_tiles, mt, nt);
+            tile_coords(t, p.m_tiles, p.n_tiles, p.group_m, mt, nt);
             if (!mbar_wait_sleepy(&sm.acc_full[acc], acc_phase, &sm.abort, 0x0521, true)) sm.epi_fail = 1;
             named_sync(1, 128);
             if (*(volatile int*)&sm.epi_fail) break;
@@ -486,6 +493,15 @@ static int launch(const void* A, const void* B, void* D, int M, int N, int K, cu
     p.n_tiles = (N + 255) / 256;
     p.scale_a = scale_a;
     p.scale_b = scale_b;
+    {
+        // As many pair-tiles per raster group as keep the group's A panels
+        // within the budget: 16 for FP8 / INT8 at K = 8192, 8 for BF16 / FP16,
+        // 4 for TF32. Wider groups re-read B less often; narrower ones keep A
+        // resident in L2 across the group's walk along N.
+        const size_t panel = (size_t)256 * (size_t)K * (size_t)C::kInBytes;
+        const size_t g = panel ? kPanelBudget / panel : (size_t)kMaxGroupM;
+        p.group_m = (int)(g < 1 ? 1 : g > (size_t)kMaxGroupM ? (size_t)kMaxGroupM : g);
+    }
     p.k_stages = (K + C::kRowElems * kSlabs - 1) / (C::kRowElems * kSlabs);
     memset(&tmD, 0, sizeof(tmD));
     p.tma_store = ((size_t)M * C::kOutBytes) % 16 == 0 && aligned16(D);
