@@ -62,13 +62,16 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["memstream", "sgemm", "fp8", "nvfp4", "bf16", "f16", "tf32", "i8",
-                                           "powervirus"],
+                                           "powervirus", "fabric"],
                     default="memstream")
     ap.add_argument("--kernel", choices=["vec4", "bulk"], default="bulk",
                     help="memstream kernel variant")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--fabric", choices=["nccl", "gplk"], default="nccl",
+                    help="powervirus fabric step: NCCL all_reduce, or gplk_fabric_allreduce_bf16 over NVLink peers")
+    ap.add_argument("--fabric-mib", type=int, default=256, help="fabric allreduce size (BF16), MiB")
     ap.add_argument("--mix", default="4,1,2", help="powervirus role weights tensor,fma,dram[,sfu,int32,smem,l2,atomic]")
     ap.add_argument("--budget-us", type=float, default=1000.0, help="powervirus launch time box")
     ap.add_argument("--duty-on-ms", type=float, default=100.0)
@@ -538,7 +541,16 @@ def bench_powervirus(args, dist: Dist) -> dict:
     cfg.inner = 256
     cfg.budget_ns = int(args.budget_us * 1e3)
     stream = torch.cuda.current_stream(dev)
-    ar = torch.ones((128 << 20,), dtype=torch.bfloat16, device=dev)  # 256 MiB
+    ar_count = (args.fabric_mib << 20) // 2
+    fab = None
+    if dist.world > 1 and args.fabric == "gplk":
+        from gplk.fabric import Fabric
+
+        fab = Fabric(dist.pg.group.WORLD, ar_count * 2)
+        ar = fab.tensor(ar_count)
+        ar.fill_(1.0)
+    else:
+        ar = torch.ones((ar_count,), dtype=torch.bfloat16, device=dev)
     ar_bytes = ar.numel() * 2
 
     def launch():
@@ -547,7 +559,12 @@ def bench_powervirus(args, dist: Dist) -> dict:
     def sync():
         torch.cuda.synchronize(dev)
 
-    allreduce = (lambda: dist.pg.all_reduce(ar)) if dist.world > 1 else None
+    if dist.world == 1:
+        allreduce = None
+    elif fab is not None:
+        allreduce = lambda: fab.allreduce_bf16(ar_count, stream=stream)  # noqa: E731
+    else:
+        allreduce = lambda: dist.pg.all_reduce(ar)  # noqa: E731
     on_ms, off_ms = args.duty_on_ms, args.duty_off_ms
     rung.run_duty_cycles(max(args.warmup, 3), on_ms, off_ms, launch, sync, allreduce, barrier=dist.barrier)
     sampler = ClockSampler(dist.local, period_s=0.01)
@@ -580,6 +597,12 @@ def bench_powervirus(args, dist: Dist) -> dict:
     node_level_w = dist.sum(level_w)
     fabric_s = sorted(log.fabric_s)[len(log.fabric_s) // 2] if log.fabric_s else 0.0
     clocks = sampler.summary()
+    if fab is not None:
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        fab.close()
+    fabric_impl = "gplk_fabric_allreduce_bf16 (NVLink peer loads/stores)" if fab is not None else "NCCL all_reduce"
+    fabric_launches = args.steps if fab is not None else 0
     return {
         "metric": "powervirus sustained power % of enforced limit" if continuous
         else "powervirus burst plateau (p95) power % of enforced limit",
@@ -591,18 +614,84 @@ def bench_powervirus(args, dist: Dist) -> dict:
                                f"{on_ms:g} ms on / {off_ms:g} ms off; 256 MiB BF16 allreduce per cycle",
                    "mix_tensor_fma_dram_sfu_int32_smem_l2_atomic": weights, "warps_per_64": counts,
                    "launch_budget_us": args.budget_us,
-                   "parallelism": f"replicas x{dist.world} in phase, NCCL allreduce per cycle"},
+                   "parallelism": f"replicas x{dist.world} in phase, {fabric_impl} per cycle"
+                   if dist.world > 1 else "single GPU, no fabric step"},
         "power": {"level_w": round(level_w, 1), "avg_w": round(sum(watts) / len(watts), 1) if watts else None,
                   "p5_w": round(pct_at(0.05), 1), "p95_w": round(pct_at(0.95), 1),
                   "min_w": round(watts[0], 1) if watts else None, "max_w": round(watts[-1], 1) if watts else None,
                   "swing_p95_p5_w": round(pct_at(0.95) - pct_at(0.05), 1),
                   "node_level_sum_w": round(node_level_w, 1), "enforced_limit_w": limit,
                   "samples": len(watts), "source": "nvml instantaneous power, 10 ms"},
-        "fabric": {"allreduce_bytes": ar_bytes if allreduce else 0, "median_s": round(fabric_s, 6),
+        "fabric": {"impl": fabric_impl if allreduce else None,
+                   "allreduce_bytes": ar_bytes if allreduce else 0, "median_s": round(fabric_s, 6),
                    "busbw_gbs": round(rung.allreduce_busbw_gbs(ar_bytes, fabric_s, dist.world), 1)
                    if allreduce else None},
         "clocks": clocks,
-        "gpu_launches": int(sum(log.launches)),
+        "gpu_launches": int(sum(log.launches)) + fabric_launches,
+    }
+
+
+# ------------------------------------------------------------ fabric step alone
+
+def bench_fabric(args, dist: Dist) -> dict:
+    """The powervirus cycle's fabric step on its own: an in-place BF16 sum
+    allreduce of --fabric-mib MiB across all ranks, gplk_fabric_allreduce_bf16
+    (value) against NCCL's all_reduce (reported beside it), CUDA events, max
+    over ranks. Bus bandwidth follows NCCL's convention 2 (N-1)/N x bytes / t."""
+    import torch
+    from gplk import rung
+    from gplk.fabric import Fabric
+
+    if dist.world < 2:
+        return {"metric": "fabric allreduce bus bandwidth", "unavailable": "needs 2 or more GPUs (torchrun)",
+                "n_gpus": dist.world}
+    dev = torch.device("cuda", dist.local)
+    torch.cuda.set_device(dev)
+    count = (args.fabric_mib << 20) // 2
+    fab = Fabric(dist.pg.group.WORLD, count * 2)
+    buf = fab.tensor(count)
+    g = torch.Generator(device=dev)
+    g.manual_seed(11 + dist.rank)
+    buf.copy_(torch.randn(count, device=dev, generator=g).to(torch.bfloat16))
+    ref = buf.clone()
+    stream = torch.cuda.current_stream(dev)
+    res = {}
+    for name, fn in (("gplk", lambda: fab.allreduce_bf16(count, stream=stream)),
+                     ("nccl", lambda: dist.pg.all_reduce(ref))):
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        res[name] = dist.max(e0.elapsed_time(e1)) / args.steps
+    import gplk
+
+    code, site = gplk.status_read()
+    dist.barrier()
+    fab.close()
+    if code != 0:
+        raise RuntimeError(f"device status {code} at {site:#x}")
+    nbytes = count * 2
+    bus = {k: rung.allreduce_busbw_gbs(nbytes, v / 1e3, dist.world) for k, v in res.items()}
+    link = 770.0  # measured peer copy GB/s per direction per GPU on this pool
+    return {
+        "metric": "fabric allreduce bus bandwidth", "value": round(bus["gplk"], 1), "unit": "GB/s",
+        "n_gpus": dist.world, "steps": args.steps, "warmup": max(args.warmup, 3),
+        "ms_per_step": round(res["gplk"], 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic N(0,1) BF16, seeded per rank",
+        "config": {"workload": f"in-place BF16 sum allreduce of {args.fabric_mib} MiB per rank, one process per GPU",
+                   "parallelism": f"allreduce x{dist.world}"},
+        "nccl": {"ms_per_step": round(res["nccl"], 4), "busbw_gbs": round(bus["nccl"], 1)},
+        "roofline": {"bound": "nvlink", "achieved": round(bus["gplk"], 1), "peak": link, "unit": "GB/s",
+                     "frac": round(bus["gplk"] / link, 4), "traffic": None,
+                     "peak_source": "measured peer copy per direction (pool figure)"},
+        "gpu_launches": args.steps,
     }
 
 
@@ -660,6 +749,8 @@ def main():
             line = bench_memstream(args, dist)
         elif args.workload in ("sgemm", "fp8", "nvfp4") or args.workload in NN_GEMMS:
             line = bench_gemm(args, dist)
+        elif args.workload == "fabric":
+            line = bench_fabric(args, dist)
         else:
             line = bench_powervirus(args, dist)
         if dist.rank == 0 and dist.world == 1 and not args.no_cpu and args.workload == "memstream":

@@ -8,3 +8,4 @@
 #include "gplk_powervirus.cu"
 #include "gplk_powervirus_noalloc.cu"
 #include "gplk_gemm_lt.cu"
+#include "gplk_fabric.cu"

@@ -137,6 +137,33 @@ int gplk_gemm_tf32_nn(const float *A, const float *B, float *D, int M, int N, in
 int gplk_gemm_i8_nn(const int8_t *A, const int8_t *B, int32_t *D, int M, int N, int K,
                     cudaStream_t stream);
 
+/* ------------------------------------------------------------ fabric step
+ * The powervirus cycle's fabric step: an in-place BF16 sum allreduce across
+ * the GPUs of one node (one process per GPU), as one kernel over NVLink
+ * peer memory. Replaces the ncclAllReduce of the multi-GPU rung
+ * (runner/src/workload_nccl.cu:119-291), which the cycle issues on a 256 MiB
+ * BF16 buffer. No multicast; plain peer loads and stores.
+ *
+ * Set-up, per rank, on its own device:
+ *   1. gplk_fabric_create(rank, world, bytes, &f, handle): allocates this
+ *      rank's buffer (bytes, a multiple of 16) and writes its CUDA IPC handle
+ *      (gplk_fabric_handle_bytes() bytes) to `handle`;
+ *   2. the caller exchanges the handles between ranks (all-gather, rank order);
+ *   3. gplk_fabric_connect(f, handles): maps every peer's buffer.
+ * gplk_fabric_data(f) is this rank's device buffer. Every rank then calls
+ * gplk_fabric_allreduce_bf16(f, count, stream) in the same order: count BF16
+ * elements (a multiple of 8) are summed in FP32 in rank order and rounded
+ * once to BF16, in every rank's buffer. A rank that does not arrive within
+ * 2 s makes the others return with GPLK_STATUS_DEVICE_TIMEOUT in the status
+ * word (gplk_status_read). world <= 8. */
+typedef struct gplk_fabric gplk_fabric;
+size_t gplk_fabric_handle_bytes(void);
+int gplk_fabric_create(int rank, int world, size_t bytes, gplk_fabric **out, void *handle);
+int gplk_fabric_connect(gplk_fabric *f, const void *handles);
+void *gplk_fabric_data(gplk_fabric *f);
+int gplk_fabric_allreduce_bf16(gplk_fabric *f, size_t count, cudaStream_t stream);
+int gplk_fabric_destroy(gplk_fabric *f);
+
 /* ------------------------------------------------------------ powervirus */
 
 #define GPLK_PV_ROLE_TENSOR 0  /* tcgen05 FP8 MMA into TMEM on smem-resident tiles */

@@ -172,6 +172,19 @@ def gemm_nn_i8(A: np.ndarray, B: np.ndarray, M: int, N: int, K: int, threads: in
     return C
 
 
+def allreduce_bf16_sum(inputs: list) -> np.ndarray:
+    """The fabric step's BF16 sum allreduce (ncclAllReduce with ncclSum,
+    runner/src/workload_nccl.cu:119-291, on BF16): every rank's buffer (uint16
+    BF16 bit patterns) added in FP32 in rank order 0..N-1, rounded once to
+    BF16 (RNE). Returns uint16 bit patterns."""
+    acc = None
+    for x in inputs:
+        f = (np.asarray(x, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+        acc = f.copy() if acc is None else (acc + f).astype(np.float32)
+    r = bf16_round(acc)
+    return (r.view(np.uint32) >> 16).astype(np.uint16)
+
+
 def f16_round(x: np.ndarray) -> np.ndarray:
     """Round float32 -> IEEE binary16 (RNE) -> float32."""
     return np.asarray(x, dtype=np.float32).astype(np.float16).astype(np.float32)

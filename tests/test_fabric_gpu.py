@@ -1,0 +1,69 @@
+"""The fabric step (gplk_fabric_*): an in-place BF16 sum allreduce over NVLink
+peer memory. One GPU: the single-rank path (its own buffer only) must leave
+the data bit-identical. Two or more GPUs: tests/fabric_ranks.py runs one
+process per GPU and checks every rank against the oracle (bit-exact) and
+against NCCL; skipped when fewer than two GPUs are visible."""
+from __future__ import annotations
+
+import json
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+REPO = Path(__file__).resolve().parent.parent
+
+
+def test_single_rank_is_identity(gplk, oracle, cuda):
+    import torch
+    from gplk.fabric import Fabric
+
+    count = 8 * 100003
+    fab = Fabric(None, count * 2, rank=0, world=1)
+    try:
+        x = (torch.randn(count, generator=torch.Generator().manual_seed(3)) * 8).to(torch.bfloat16)
+        buf = fab.tensor(count)
+        buf.copy_(x.cuda())
+        for _ in range(3):  # three epochs
+            fab.allreduce_bf16(count)
+        torch.cuda.synchronize()
+        got = buf.view(torch.int16).cpu().numpy()
+        assert np.array_equal(got, x.view(torch.int16).numpy())
+        ref = oracle.allreduce_bf16_sum([x.view(torch.int16).numpy().view(np.uint16)])
+        assert np.array_equal(got.view(np.uint16), ref)
+    finally:
+        fab.close()
+
+
+def test_bad_arguments(gplk, cuda):
+    from gplk.fabric import Fabric
+
+    fab = Fabric(None, 4096, rank=0, world=1)
+    try:
+        with pytest.raises(gplk.GplkError):
+            fab.allreduce_bf16(12)  # not a multiple of 8
+        with pytest.raises(gplk.GplkError):
+            fab.allreduce_bf16(4096)  # larger than the buffer
+    finally:
+        fab.close()
+
+
+@pytest.mark.skipif(int(os.environ.get("GPLK_TEST_GPUS", "0") or 0) < 2, reason="needs GPLK_TEST_GPUS >= 2 GPUs")
+def test_multi_rank_matches_oracle_and_nccl():
+    import torch
+
+    n = min(torch.cuda.device_count(), int(os.environ["GPLK_TEST_GPUS"]))
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
+           "--master-addr", "127.0.0.1", "--master-port", "29533", str(REPO / "tests/fabric_ranks.py"),
+           "--mode", "check"]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    res = subprocess.run(["timeout", "-k", "30", "300", *cmd], capture_output=True, text=True, env=env)
+    line = [l for l in res.stdout.splitlines() if l.startswith("{")]
+    assert res.returncode == 0 and line, res.stdout[-2000:] + res.stderr[-3000:]
+    out = json.loads(line[-1])
+    assert out["ok"] and out["world"] == n
