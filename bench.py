@@ -69,6 +69,9 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--phase", choices=["aligned", "staggered"], default="aligned",
+                    help="powervirus: ranks' duty cycles in phase, or spread evenly over one period "
+                         "(staggered drops the per-cycle fabric step, which would re-align them)")
     ap.add_argument("--fabric", choices=["nccl", "gplk"], default="nccl",
                     help="powervirus fabric step: NCCL all_reduce, or gplk_fabric_allreduce_bf16 over NVLink peers")
     ap.add_argument("--fabric-mib", type=int, default=256, help="fabric allreduce size (BF16), MiB")
@@ -513,6 +516,36 @@ def bench_gemm(args, dist: Dist) -> dict:
 
 # ------------------------------------------------------------ powervirus rung
 
+def node_power_summary(mon, on_ms: float, off_ms: float, phase: str) -> dict | None:
+    """Node-level power from gplk_nodemon: the sum over all GPUs of the job,
+    binned at 10 ms from the driver's buffered samples (device timestamps) and
+    from the polled instantaneous path. The swing is p95 - p5 of the node sum."""
+    if mon is None:
+        return None
+    if isinstance(mon, str):
+        return {"unavailable": mon}
+    from gplk import nodemon
+
+    mon.stop()
+    s = mon.samples()
+    out = {"phase": phase, "devices": len(mon.devices), "period_ms": on_ms + off_ms}
+    for name, src in (("buffered", nodemon.BUFFERED), ("polled", nodemon.POLLED)):
+        n = int(((s["source"] == src)).sum())
+        w = mon.node_series(src, t0=0.0, bin_s=0.01, max_bins=200000)
+        w = w[10:] if len(w) > 20 else w  # drop the first 100 ms while every device starts reporting
+        if n == 0 or len(w) == 0:
+            out[name] = {"samples": n}
+            continue
+        pct = lambda q: float(sorted(w)[min(len(w) - 1, int(q * (len(w) - 1)))])  # noqa: E731
+        out[name] = {"samples": n, "mean_w": round(float(w.mean()), 1), "p95_w": round(pct(0.95), 1),
+                     "p5_w": round(pct(0.05), 1), "swing_w": round(pct(0.95) - pct(0.05), 1),
+                     "max_w": round(float(w.max()), 1)}
+    inst = s[(s["source"] == nodemon.POLLED) & (s["instant_w"] >= 0)]
+    out["peak_instant_w_any_gpu"] = round(float(inst["instant_w"].max()), 1) if len(inst) else None
+    mon.close()
+    return out
+
+
 def bench_powervirus(args, dist: Dist) -> dict:
     """Duty-cycled powervirus on every GPU in phase; each cycle = burst of
     time-boxed launches for duty_on_ms, a 256 MiB BF16 allreduce across all
@@ -559,24 +592,38 @@ def bench_powervirus(args, dist: Dist) -> dict:
     def sync():
         torch.cuda.synchronize(dev)
 
-    if dist.world == 1:
+    staggered = args.phase == "staggered"
+    if dist.world == 1 or staggered:
         allreduce = None
     elif fab is not None:
         allreduce = lambda: fab.allreduce_bf16(ar_count, stream=stream)  # noqa: E731
     else:
         allreduce = lambda: dist.pg.all_reduce(ar)  # noqa: E731
     on_ms, off_ms = args.duty_on_ms, args.duty_off_ms
+    offset = rung.phase_offset_s(dist.rank, dist.world, on_ms, off_ms, staggered)
     rung.run_duty_cycles(max(args.warmup, 3), on_ms, off_ms, launch, sync, allreduce, barrier=dist.barrier)
     sampler = ClockSampler(dist.local, period_s=0.01)
     sampler.start()
+    # Node-level view (rank 0): every GPU of the job sampled from one process
+    # on one timebase, including the driver's buffered power samples.
+    mon = None
+    if dist.rank == 0:
+        try:
+            from gplk import nodemon
+
+            mon = nodemon.NodeMonitor(list(range(dist.world)), hz=100, drain_ms=50)
+        except Exception as exc:  # NVML or the sampler library unavailable: report without it
+            mon = str(exc)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     dist.barrier()
     e0.record(stream)
-    log = rung.run_duty_cycles(args.steps, on_ms, off_ms, launch, sync, allreduce, barrier=dist.barrier)
+    log = rung.run_duty_cycles(args.steps, on_ms, off_ms, launch, sync, allreduce, barrier=dist.barrier,
+                               start_offset_s=offset)
     e1.record(stream)
     torch.cuda.synchronize(dev)
     dist.barrier()
     sampler.stop()
+    node = node_power_summary(mon, on_ms, off_ms, args.phase)
     code, site = gplk.status_read()
     if code != 0:
         raise RuntimeError(f"device status {code} at {site:#x}")
@@ -611,17 +658,21 @@ def bench_powervirus(args, dist: Dist) -> dict:
         "ms_per_step": round(ms_max / args.steps, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "e4m3+f32", "data": "synthetic: 0x3c-filled 2 GiB stream, E4M3 1.0 tiles",
         "config": {"workload": "powervirus duty cycle: in-kernel tcgen05 FP8 + FFMA + TMA-bulk HBM streaming; "
-                               f"{on_ms:g} ms on / {off_ms:g} ms off; 256 MiB BF16 allreduce per cycle",
+                               f"{on_ms:g} ms on / {off_ms:g} ms off; {args.fabric_mib} MiB BF16 allreduce per cycle",
                    "mix_tensor_fma_dram_sfu_int32_smem_l2_atomic": weights, "warps_per_64": counts,
                    "launch_budget_us": args.budget_us,
+                   "phase": args.phase,
                    "parallelism": f"replicas x{dist.world} in phase, {fabric_impl} per cycle"
-                   if dist.world > 1 else "single GPU, no fabric step"},
+                   if dist.world > 1 and not staggered else
+                   (f"replicas x{dist.world} staggered over one period, no fabric step" if staggered
+                    else "single GPU, no fabric step")},
         "power": {"level_w": round(level_w, 1), "avg_w": round(sum(watts) / len(watts), 1) if watts else None,
                   "p5_w": round(pct_at(0.05), 1), "p95_w": round(pct_at(0.95), 1),
                   "min_w": round(watts[0], 1) if watts else None, "max_w": round(watts[-1], 1) if watts else None,
                   "swing_p95_p5_w": round(pct_at(0.95) - pct_at(0.05), 1),
                   "node_level_sum_w": round(node_level_w, 1), "enforced_limit_w": limit,
                   "samples": len(watts), "source": "nvml instantaneous power, 10 ms"},
+        "node": node,
         "fabric": {"impl": fabric_impl if allreduce else None,
                    "allreduce_bytes": ar_bytes if allreduce else 0, "median_s": round(fabric_s, 6),
                    "busbw_gbs": round(rung.allreduce_busbw_gbs(ar_bytes, fabric_s, dist.world), 1)

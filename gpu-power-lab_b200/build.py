@@ -64,6 +64,27 @@ def build(verbose: bool = False, force: bool = False) -> Path:
     return LIB
 
 
+NODEMON = PKG / "libgplk_nodemon.so"
+
+
+def build_nodemon(force: bool = False) -> Path:
+    """libgplk_nodemon.so: the node-level NVML sampler (host C, no CUDA code;
+    NVML is loaded at run time with dlopen)."""
+    src = CSRC / "gplk_nodemon.c"
+    hdr = REPO / "include" / "gplk_nodemon.h"
+    if not force and NODEMON.exists() and NODEMON.stat().st_mtime >= max(src.stat().st_mtime, hdr.stat().st_mtime):
+        return NODEMON
+    cmd = ["gcc", "-std=gnu11", "-O2", "-Wall", "-fPIC", "-shared", "-I", "/usr/local/cuda/include",
+           "-o", str(NODEMON), str(src), "-ldl", "-lpthread"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        sys.stderr.write(res.stdout + res.stderr)
+        raise RuntimeError("gcc failed building libgplk_nodemon.so")
+    return NODEMON
+
+
 if __name__ == "__main__":
     build(verbose="--verbose" in sys.argv, force=True)
+    build_nodemon(force=True)
     print(LIB)
+    print(NODEMON)

@@ -35,14 +35,20 @@ class CycleLog:
 def run_duty_cycles(cycles: int, on_ms: float, off_ms: float, launch: Callable[[], None], sync: Callable[[], None],
                     allreduce: Callable[[], None] | None, barrier: Callable[[], None] | None = None,
                     sync_every: int = 8, clock: Callable[[], float] = time.time,
-                    sleep: Callable[[float], None] = time.sleep) -> CycleLog:
+                    sleep: Callable[[float], None] = time.sleep, start_offset_s: float = 0.0) -> CycleLog:
     """Run `cycles` duty cycles: launch kernels back to back for on_ms
     (syncing every `sync_every` launches, as the reference's batches do),
     then the fabric allreduce, then sleep off_ms. `barrier` (optional) aligns
-    the ranks once before the first cycle so the cycles run in phase."""
+    the ranks once before the first cycle so the cycles run in phase;
+    `start_offset_s` then delays this rank's first cycle, which staggers the
+    ranks' phases (rank r of N at r x period / N spreads them evenly). With a
+    fabric step every cycle the collective re-aligns the ranks, so staggering
+    is meaningful without one (allreduce None)."""
     log = CycleLog()
     if barrier is not None:
         barrier()
+    if start_offset_s > 0:
+        sleep(start_offset_s)
     for _ in range(cycles):
         t0 = clock()
         log.burst_start.append(t0)
@@ -74,6 +80,14 @@ def allreduce_busbw_gbs(nbytes: int, seconds: float, world: int) -> float:
     if seconds <= 0 or world < 1:
         return 0.0
     return 2.0 * (world - 1) / world * nbytes / seconds / 1e9
+
+
+def phase_offset_s(rank: int, world: int, on_ms: float, off_ms: float, staggered: bool) -> float:
+    """Start offset of `rank` for a staggered duty cycle: ranks spread evenly
+    over one period; 0 when aligned."""
+    if not staggered or world <= 1:
+        return 0.0
+    return rank * (on_ms + off_ms) / 1e3 / world
 
 
 def window_power(samples: list[tuple[float, float]], windows: list[tuple[float, float]]) -> list[float]:

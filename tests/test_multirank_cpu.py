@@ -76,3 +76,54 @@ def test_busbw_and_windows():
     assert rung.allreduce_busbw_gbs(1_000_000_000, 1.0, 8) == pytest.approx(1.75)
     samples = [(0.5, 100.0), (1.5, 900.0), (2.5, 200.0), (3.2, 950.0)]
     assert rung.window_power(samples, [(1.0, 2.0), (3.0, 4.0)]) == [900.0, 950.0]
+
+
+def _stagger_worker(rank: int, world: int, port: int, out):
+    os.environ.update({"RANK": str(rank), "WORLD_SIZE": str(world), "LOCAL_RANK": str(rank),
+                       "MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port)})
+    import sys
+    from pathlib import Path
+
+    repo = Path(__file__).resolve().parent.parent
+    sys.path[:0] = [str(repo), str(repo / "gpu-power-lab_b200")]
+    import bench
+    from gplk import rung
+
+    d = bench.Dist(world, backend="gloo")
+    on_ms, off_ms = 40.0, 40.0
+    off = rung.phase_offset_s(rank, world, on_ms, off_ms, staggered=True)
+    log = rung.run_duty_cycles(cycles=3, on_ms=on_ms, off_ms=off_ms, launch=lambda: None, sync=lambda: None,
+                               allreduce=None, barrier=d.barrier, start_offset_s=off)
+    d.close()
+    out.put((rank, off, log.burst_start))
+
+
+def test_staggered_phases_on_cpu_ranks():
+    """Staggered duty cycles: after the shared barrier, rank r of N starts
+    r x period / N later, so the two ranks' bursts interleave."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_stagger_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    (_, off0, starts0), (_, off1, starts1) = res
+    assert off0 == 0.0 and off1 == pytest.approx(0.04)
+    # rank 1's bursts start half a period (40 ms) after rank 0's, within scheduling slack
+    lag = [b - a for a, b in zip(starts0, starts1)]
+    assert all(0.025 <= x <= 0.075 for x in lag), lag
+
+
+def test_phase_offsets():
+    import sys
+    from pathlib import Path
+
+    sys.path.insert(0, str(Path(__file__).resolve().parent.parent / "gpu-power-lab_b200"))
+    from gplk import rung
+
+    assert rung.phase_offset_s(3, 8, 100, 100, staggered=False) == 0.0
+    assert [rung.phase_offset_s(r, 4, 100, 100, True) for r in range(4)] == pytest.approx([0, 0.05, 0.1, 0.15])
