@@ -36,7 +36,7 @@ def _run(gplk, pa, sfa, pb, sfb, alpha, K, cuda):
 
 
 @pytest.mark.parametrize("mnk", [(128, 256, 256), (256, 256, 512), (512, 768, 1024), (128, 384, 512),
-                                 (200, 300, 256), (1024, 1024, 2048)])
+                                 (200, 300, 256), (1024, 1024, 2048), (384, 512, 768), (136, 264, 1280)])
 def test_nvfp4_full_vs_oracle(mnk, gplk, oracle, cuda):
     M, N, K = mnk
     pa, sfa, pb, sfb, alpha = _operands(oracle, M, N, K, seed=M + 3 * N)
