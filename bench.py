@@ -42,7 +42,7 @@ NCU_TRAFFIC = {
     "memstream_vec4": 12.58e9,  # profiles/memstream_triad_2p30.md: 8 x 1.573 GB (3 x 2^27 capture)
     "memstream_bulk": 12.58e9,  # profiles/memstream_triad_2p30.md: 8 x 1.572 GB (3 x 2^27 capture)
     "sgemm": 8.4e6,             # profiles/sgemm_f32_1024.md
-    "fp8": 356.7e6,             # profiles/gemm_fp8_8192.md
+    "fp8": 361.7e6,             # profiles/gemm_fp8_8192.md
     "nvfp4": 1343.6e6,          # profiles/gemm_nvfp4_16384.md
 }
 

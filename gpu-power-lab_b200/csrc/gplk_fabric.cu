@@ -81,6 +81,24 @@ __device__ __forceinline__ void add_bf16x2(float& lo, float& hi, uint32_t v) {
     hi += __uint_as_float(v & 0xFFFF0000u);
 }
 
+// FP32 elements: four per vector, summed in rank order.
+template <int W>
+__device__ __forceinline__ uint4 reduce_vec_f32(const Args& a, size_t i) {
+    uint4 v[W];
+#pragma unroll
+    for (int q = 0; q < W; ++q) v[q] = a.src[q][i];
+    float s0 = __uint_as_float(v[0].x), s1 = __uint_as_float(v[0].y), s2 = __uint_as_float(v[0].z),
+          s3 = __uint_as_float(v[0].w);
+#pragma unroll
+    for (int q = 1; q < W; ++q) {
+        s0 += __uint_as_float(v[q].x);
+        s1 += __uint_as_float(v[q].y);
+        s2 += __uint_as_float(v[q].z);
+        s3 += __uint_as_float(v[q].w);
+    }
+    return make_uint4(__float_as_uint(s0), __float_as_uint(s1), __float_as_uint(s2), __float_as_uint(s3));
+}
+
 template <int W>
 __device__ __forceinline__ uint4 reduce_vec(const Args& a, size_t i) {
     uint4 v[W];
@@ -106,8 +124,8 @@ __device__ __forceinline__ uint4 reduce_vec(const Args& a, size_t i) {
                       pack_bf16x2(s[6], s[7]));
 }
 
-template <int W>
-__global__ void __launch_bounds__(kThreads) allreduce_bf16_kernel(const Args a) {
+template <int W, bool F32>
+__global__ void __launch_bounds__(kThreads) allreduce_kernel(const Args a) {
     unsigned* my_flags = a.flags[a.rank];
     // ---- entry: announce, then wait for every rank (one thread per block)
     if (blockIdx.x == 0 && threadIdx.x < (unsigned)W) st_release_sys(a.flags[threadIdx.x] + kEntry + a.rank, a.epoch);
@@ -124,7 +142,7 @@ __global__ void __launch_bounds__(kThreads) allreduce_bf16_kernel(const Args a) 
         const size_t hi = lo + a.chunk16 < a.n16 ? lo + a.chunk16 : a.n16;
         const size_t stride = (size_t)gridDim.x * blockDim.x;
         for (size_t i = lo + (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < hi; i += stride) {
-            const uint4 r = reduce_vec<W>(a, i);
+            const uint4 r = F32 ? reduce_vec_f32<W>(a, i) : reduce_vec<W>(a, i);
 #pragma unroll
             for (int q = 0; q < W; ++q) a.dst[q][i] = r;
         }
@@ -154,6 +172,7 @@ struct gplk_fabric {
     unsigned char* base = nullptr;  // this rank's region: flags, then data
     unsigned char* peer[gplk::fabric::kMaxRanks] = {};
     bool connected = false;
+    bool local = false;  // peers are this process's own allocations (no IPC mappings to close)
     unsigned epoch = 0;
 };
 
@@ -217,40 +236,130 @@ extern "C" int gplk_fabric_connect(gplk_fabric* f, const void* handles) {
     return GPLK_STATUS_OK;
 }
 
+extern "C" int gplk_fabric_create_local(int ndev, const int* devices, size_t bytes, gplk_fabric** out) {
+    using namespace gplk;
+    if (!out || !devices || ndev < 1 || ndev > fabric::kMaxRanks || bytes == 0 || bytes % 16 != 0)
+        return GPLK_STATUS_BAD_ARG;
+    int cur = 0;
+    cudaGetDevice(&cur);
+    for (int i = 0; i < ndev; ++i) out[i] = nullptr;
+    int st = GPLK_STATUS_OK;
+    for (int i = 0; i < ndev && st == GPLK_STATUS_OK; ++i) {
+        if (cudaSetDevice(devices[i]) != cudaSuccess) {
+            st = GPLK_STATUS_BAD_ARG;
+            break;
+        }
+        DeviceInfo d;
+        st = require_sm100(&d);
+        if (st != GPLK_STATUS_OK) break;
+        gplk_fabric* f = new gplk_fabric();
+        f->rank = i;
+        f->world = ndev;
+        f->bytes = bytes;
+        f->device = devices[i];
+        f->blocks = d.sm_count;
+        f->local = true;
+        void* p = nullptr;
+        if (cudaMalloc(&p, fabric::kFlagBytes + bytes) != cudaSuccess ||
+            cudaMemset(p, 0, fabric::kFlagBytes) != cudaSuccess) {
+            cudaGetLastError();
+            if (p) cudaFree(p);
+            delete f;
+            st = GPLK_STATUS_CUDA_ERROR;
+            break;
+        }
+        f->base = static_cast<unsigned char*>(p);
+        out[i] = f;
+        for (int j = 0; j < ndev; ++j) {  // peer access to every other device
+            if (j == i) continue;
+            const cudaError_t e = cudaDeviceEnablePeerAccess(devices[j], 0);
+            if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled) {
+                cudaGetLastError();
+                st = GPLK_STATUS_CUDA_ERROR;
+                break;
+            }
+            cudaGetLastError();
+        }
+    }
+    if (st == GPLK_STATUS_OK) {
+        for (int i = 0; i < ndev; ++i) {
+            for (int q = 0; q < ndev; ++q) out[i]->peer[q] = out[q]->base;
+            out[i]->connected = true;
+        }
+    } else {
+        for (int i = 0; i < ndev; ++i) {
+            if (!out[i]) continue;
+            cudaSetDevice(out[i]->device);
+            cudaFree(out[i]->base);
+            delete out[i];
+            out[i] = nullptr;
+        }
+    }
+    cudaSetDevice(cur);
+    return st;
+}
+
 extern "C" void* gplk_fabric_data(gplk_fabric* f) { return f ? f->base + gplk::fabric::kFlagBytes : nullptr; }
 
-extern "C" int gplk_fabric_allreduce_bf16(gplk_fabric* f, size_t count, cudaStream_t stream) {
-    using namespace gplk;
-    namespace fb = gplk::fabric;
-    if (!f || !f->connected || count % 8 != 0 || count * 2 > f->bytes) return GPLK_STATUS_BAD_ARG;
-    if (count == 0) return GPLK_STATUS_OK;
-    fb::Args a;
+namespace gplk {
+namespace fabric {
+
+template <bool F32>
+static const void* kernel_for(int world) {
+    switch (world) {
+        case 1: return (const void*)allreduce_kernel<1, F32>;
+        case 2: return (const void*)allreduce_kernel<2, F32>;
+        case 3: return (const void*)allreduce_kernel<3, F32>;
+        case 4: return (const void*)allreduce_kernel<4, F32>;
+        case 5: return (const void*)allreduce_kernel<5, F32>;
+        case 6: return (const void*)allreduce_kernel<6, F32>;
+        case 7: return (const void*)allreduce_kernel<7, F32>;
+        default: return (const void*)allreduce_kernel<8, F32>;
+    }
+}
+
+// One in-place allreduce of `n16` 16-byte vectors on this rank's device.
+template <bool F32>
+static int launch_allreduce(gplk_fabric* f, size_t n16, cudaStream_t stream) {
+    Args a;
     memset(&a, 0, sizeof(a));
     for (int q = 0; q < f->world; ++q) {
-        a.src[q] = reinterpret_cast<const uint4*>(f->peer[q] + fb::kFlagBytes);
-        a.dst[q] = reinterpret_cast<uint4*>(f->peer[q] + fb::kFlagBytes);
+        a.src[q] = reinterpret_cast<const uint4*>(f->peer[q] + kFlagBytes);
+        a.dst[q] = reinterpret_cast<uint4*>(f->peer[q] + kFlagBytes);
         a.flags[q] = reinterpret_cast<unsigned*>(f->peer[q]);
     }
     a.rank = f->rank;
     a.world = f->world;
-    a.n16 = count / 8;
-    a.chunk16 = (a.n16 + (size_t)f->world - 1) / (size_t)f->world;
+    a.n16 = n16;
+    a.chunk16 = (n16 + (size_t)f->world - 1) / (size_t)f->world;
     a.epoch = ++f->epoch;
     a.budget_ns = 2000000000ull;
     void* args[] = {&a};
-    const void* fn = nullptr;
-    switch (f->world) {
-        case 1: fn = (const void*)fb::allreduce_bf16_kernel<1>; break;
-        case 2: fn = (const void*)fb::allreduce_bf16_kernel<2>; break;
-        case 3: fn = (const void*)fb::allreduce_bf16_kernel<3>; break;
-        case 4: fn = (const void*)fb::allreduce_bf16_kernel<4>; break;
-        case 5: fn = (const void*)fb::allreduce_bf16_kernel<5>; break;
-        case 6: fn = (const void*)fb::allreduce_bf16_kernel<6>; break;
-        case 7: fn = (const void*)fb::allreduce_bf16_kernel<7>; break;
-        default: fn = (const void*)fb::allreduce_bf16_kernel<8>; break;
-    }
-    const cudaError_t e = cudaLaunchCooperativeKernel(fn, dim3((unsigned)f->blocks), dim3(fb::kThreads), args, 0, stream);
+    // The launch goes to the fabric's device (a single process may drive several).
+    int cur = 0;
+    cudaGetDevice(&cur);
+    if (cur != f->device) cudaSetDevice(f->device);
+    const cudaError_t e = cudaLaunchCooperativeKernel(kernel_for<F32>(f->world), dim3((unsigned)f->blocks),
+                                                      dim3(kThreads), args, 0, stream);
+    if (cur != f->device) cudaSetDevice(cur);
     return launch_status(e);
+}
+
+}  // namespace fabric
+}  // namespace gplk
+
+extern "C" int gplk_fabric_allreduce_f32(gplk_fabric* f, size_t count, cudaStream_t stream) {
+    using namespace gplk;
+    if (!f || !f->connected || count % 4 != 0 || count * 4 > f->bytes) return GPLK_STATUS_BAD_ARG;
+    if (count == 0) return GPLK_STATUS_OK;
+    return fabric::launch_allreduce<true>(f, count / 4, stream);
+}
+
+extern "C" int gplk_fabric_allreduce_bf16(gplk_fabric* f, size_t count, cudaStream_t stream) {
+    using namespace gplk;
+    if (!f || !f->connected || count % 8 != 0 || count * 2 > f->bytes) return GPLK_STATUS_BAD_ARG;
+    if (count == 0) return GPLK_STATUS_OK;
+    return fabric::launch_allreduce<false>(f, count / 8, stream);
 }
 
 extern "C" int gplk_fabric_destroy(gplk_fabric* f) {
@@ -258,8 +367,9 @@ extern "C" int gplk_fabric_destroy(gplk_fabric* f) {
     int dev = 0;
     cudaGetDevice(&dev);
     cudaSetDevice(f->device);
-    for (int q = 0; q < f->world; ++q)
-        if (q != f->rank && f->peer[q]) cudaIpcCloseMemHandle(f->peer[q]);
+    if (!f->local)
+        for (int q = 0; q < f->world; ++q)
+            if (q != f->rank && f->peer[q]) cudaIpcCloseMemHandle(f->peer[q]);
     if (f->base) cudaFree(f->base);
     cudaSetDevice(dev);
     delete f;

@@ -36,6 +36,11 @@ def _bind():
     L.gplk_fabric_allreduce_bf16.argtypes = [_p, ctypes.c_size_t, _p]
     L.gplk_fabric_destroy.restype = ctypes.c_int
     L.gplk_fabric_destroy.argtypes = [_p]
+    L.gplk_fabric_allreduce_f32.restype = ctypes.c_int
+    L.gplk_fabric_allreduce_f32.argtypes = [_p, ctypes.c_size_t, _p]
+    L.gplk_fabric_create_local.restype = ctypes.c_int
+    L.gplk_fabric_create_local.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.c_size_t,
+                                           ctypes.POINTER(_p)]
     L._fabric_bound = True
     return L
 
@@ -43,9 +48,56 @@ def _bind():
 class _CudaArray:
     """Minimal __cuda_array_interface__ holder so torch can view the buffer."""
 
-    def __init__(self, ptr: int, count: int):
-        self.__cuda_array_interface__ = {"shape": (count,), "typestr": "<i2", "data": (ptr, False),
+    def __init__(self, ptr: int, count: int, typestr: str = "<i2"):
+        self.__cuda_array_interface__ = {"shape": (count,), "typestr": typestr, "data": (ptr, False),
                                          "version": 3, "strides": None}
+
+
+class LocalFabric:
+    """One GPU's side of a single-process fabric (gplk_fabric_create_local):
+    this process drives every GPU of the group, as the reference's NCCL rung
+    does with ncclCommInitAll. Build the group with `local_group`."""
+
+    def __init__(self, handle: ctypes.c_void_p, device: int, nbytes: int):
+        self._f = handle
+        self.device = device
+        self.nbytes = nbytes
+
+    def data_ptr(self) -> int:
+        return int(_bind().gplk_fabric_data(self._f))
+
+    def tensor(self, count: int, dtype=None):
+        import torch
+
+        dtype = dtype or torch.bfloat16
+        es = 2 if dtype == torch.bfloat16 else 4
+        assert count * es <= self.nbytes
+        with torch.cuda.device(self.device):
+            t = torch.as_tensor(_CudaArray(self.data_ptr(), count, "<i2" if es == 2 else "<f4"),
+                                device=f"cuda:{self.device}")
+        return t.view(torch.bfloat16) if es == 2 else t
+
+    def allreduce(self, count: int, dtype=None, stream=None) -> None:
+        import torch
+
+        fn = "gplk_fabric_allreduce_f32" if dtype == torch.float32 else "gplk_fabric_allreduce_bf16"
+        s = stream.cuda_stream if stream is not None else torch.cuda.current_stream(self.device).cuda_stream
+        gplk._check(fn, getattr(_bind(), fn)(self._f, int(count), s))
+
+    def close(self) -> None:
+        if self._f:
+            _bind().gplk_fabric_destroy(self._f)
+            self._f = _p()
+
+
+def local_group(devices, nbytes: int) -> list[LocalFabric]:
+    """Fabrics over `devices` driven from this one process."""
+    L = _bind()
+    n = len(devices)
+    devs = (ctypes.c_int * n)(*[int(d) for d in devices])
+    outs = (_p * n)()
+    gplk._check("gplk_fabric_create_local", L.gplk_fabric_create_local(n, devs, int(nbytes), outs))
+    return [LocalFabric(_p(outs[i]), int(devices[i]), int(nbytes)) for i in range(n)]
 
 
 class Fabric:

@@ -162,6 +162,16 @@ int gplk_fabric_create(int rank, int world, size_t bytes, gplk_fabric **out, voi
 int gplk_fabric_connect(gplk_fabric *f, const void *handles);
 void *gplk_fabric_data(gplk_fabric *f);
 int gplk_fabric_allreduce_bf16(gplk_fabric *f, size_t count, cudaStream_t stream);
+/* The same with FP32 elements (count a multiple of 4), the reference NCCL
+ * rung's data type (ncclFloat, runner/src/workload_nccl.cu:127-128). */
+int gplk_fabric_allreduce_f32(gplk_fabric *f, size_t count, cudaStream_t stream);
+/* Single process driving several GPUs, as the reference's NCCL rung does
+ * (ncclCommInitAll over all devices, runner/src/workload_nccl.cu:18-23): one
+ * fabric per listed device in out[0..ndev-1], buffers allocated on each
+ * device and mapped through peer access (no IPC). Call the allreduce once
+ * per fabric, each on a stream of that fabric's device; the call launches
+ * on the fabric's device whatever device is current. */
+int gplk_fabric_create_local(int ndev, const int *devices, size_t bytes, gplk_fabric **out);
 int gplk_fabric_destroy(gplk_fabric *f);
 
 /* ------------------------------------------------------------ powervirus */

@@ -67,3 +67,59 @@ def test_multi_rank_matches_oracle_and_nccl():
     assert res.returncode == 0 and line, res.stdout[-2000:] + res.stderr[-3000:]
     out = json.loads(line[-1])
     assert out["ok"] and out["world"] == n
+
+
+def test_local_group_single_gpu_f32_identity(gplk, cuda):
+    import torch
+    from gplk.fabric import local_group
+
+    (f,) = local_group([0], 1 << 20)
+    try:
+        count = 4 * 60001
+        x = torch.randn(count, generator=torch.Generator().manual_seed(5))
+        buf = f.tensor(count, torch.float32)
+        buf.copy_(x.cuda())
+        f.allreduce(count, torch.float32)
+        torch.cuda.synchronize()
+        assert torch.equal(buf.cpu(), x)
+    finally:
+        f.close()
+
+
+def test_local_group_all_gpus_matches_oracle(gplk, oracle):
+    """One process driving every visible GPU (skipped with fewer than two):
+    FP32 and BF16 sums in rank order, bit-exact against the oracle."""
+    import torch
+    from gplk.fabric import local_group
+
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs 2 or more GPUs in this process")
+    n = min(n, 8)
+    group = local_group(list(range(n)), 64 << 20)
+    try:
+        for dtype, count in ((torch.float32, 4 * (n * 100003 + 1)), (torch.bfloat16, 8 * (n * 70001 + 3))):
+            xs = [torch.randn(count, generator=torch.Generator().manual_seed(100 + r)).to(dtype) for r in range(n)]
+            for f, x in zip(group, xs):
+                f.tensor(count, dtype).copy_(x.to(f"cuda:{f.device}"))
+            for f in group:
+                torch.cuda.synchronize(f.device)
+            for f in group:
+                f.allreduce(count, dtype)
+            for f in group:
+                torch.cuda.synchronize(f.device)
+            if dtype == torch.float32:
+                want = xs[0].numpy().copy()
+                for x in xs[1:]:
+                    want = (want + x.numpy()).astype(np.float32)
+                for f in group:
+                    assert np.array_equal(f.tensor(count, dtype).cpu().numpy().view(np.uint32), want.view(np.uint32))
+            else:
+                want = oracle.allreduce_bf16_sum([x.view(torch.int16).numpy().view(np.uint16) for x in xs])
+                for f in group:
+                    assert np.array_equal(f.tensor(count, dtype).view(torch.int16).cpu().numpy().view(np.uint16), want)
+        code, site = gplk.status_read()
+        assert code == 0, (code, hex(site))
+    finally:
+        for f in group:
+            f.close()
