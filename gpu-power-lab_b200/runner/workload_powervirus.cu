@@ -10,7 +10,9 @@
  * warp-synchronous wmma role. With --tensor-backend cublas the tensor role
  * leaves the kernel, as in the reference, and GEMMs run on a concurrent
  * stream: fp8/fp4 through gpl_lt_* (libgplk tcgen05 GEMMs, now including a
- * working NVFP4), other precisions through cublasGemmEx with beta = 1.
+ * working NVFP4), bf16/fp16/tf32/int8 through libgplk's tcgen05 NN GEMMs
+ * (D = A * B; GPL_GEMM_BACKEND=cublas keeps the reference's cublasGemmEx
+ * with beta = 1), fp32 and fp64 through cublasGemmEx with beta = 1.
  * Ramped duty edges shape the kernel's block count.
  */
 #include "workload.h"
@@ -32,6 +34,8 @@ namespace {
 struct TensorStream {
     gpl_lt_gemm_t lt;
     bool use_lt = false;
+    bool use_gplk = false;  // tcgen05 NN GEMM of the rung's precision
+    gpl_prec_t prec = GPL_PREC_FP16;
     cublasHandle_t h = nullptr;
     cudaStream_t stream = nullptr;
     void *dA = nullptr, *dB = nullptr, *dC = nullptr;
@@ -58,6 +62,13 @@ int tensor_stream_init(gpl_workload_ctx_t *ctx, TensorStream *ts) {
         return 0;
     }
     size_t in_b = 2, out_b = 2;
+    ts->prec = a->precision;
+    {
+        const char *b = getenv("GPL_GEMM_BACKEND");
+        const bool cublas = b && !strcmp(b, "cublas");
+        ts->use_gplk = !cublas && (a->precision == GPL_PREC_BF16 || a->precision == GPL_PREC_FP16 ||
+                                   a->precision == GPL_PREC_TF32 || a->precision == GPL_PREC_INT8);
+    }
     switch (a->precision) {
         case GPL_PREC_FP32: ts->in_t = ts->out_t = CUDA_R_32F; ts->comp_t = CUBLAS_COMPUTE_32F; in_b = out_b = 4; break;
         case GPL_PREC_TF32: ts->in_t = ts->out_t = CUDA_R_32F; ts->comp_t = CUBLAS_COMPUTE_32F_FAST_TF32; in_b = out_b = 4; break;
@@ -75,6 +86,10 @@ int tensor_stream_init(gpl_workload_ctx_t *ctx, TensorStream *ts) {
     cudaMemset(ts->dA, 0x3c, nn * in_b);
     cudaMemset(ts->dB, 0x3c, nn * in_b);
     cudaMemset(ts->dC, 0, nn * out_b);
+    if (ts->use_gplk) {
+        ts->active = true;
+        return 0;
+    }
     if (cublasCreate(&ts->h) != CUBLAS_STATUS_SUCCESS) {
         ctx->error = "cublasCreate failed";
         return -1;
@@ -89,6 +104,32 @@ int tensor_stream_init(gpl_workload_ctx_t *ctx, TensorStream *ts) {
 int tensor_stream_enqueue(TensorStream *ts, int count) {
     if (!ts->active || count <= 0) return 0;
     if (ts->use_lt) return gpl_lt_enqueue(&ts->lt, count);
+    if (ts->use_gplk) {
+        const int n = ts->n;
+        for (int i = 0; i < count; i++) {
+            int st = GPLK_STATUS_BAD_ARG;
+            switch (ts->prec) {
+                case GPL_PREC_BF16:
+                    st = gplk_gemm_bf16_nn((const uint16_t *)ts->dA, (const uint16_t *)ts->dB, (uint16_t *)ts->dC, n,
+                                           n, n, ts->stream);
+                    break;
+                case GPL_PREC_FP16:
+                    st = gplk_gemm_f16_nn((const uint16_t *)ts->dA, (const uint16_t *)ts->dB, (uint16_t *)ts->dC, n,
+                                          n, n, ts->stream);
+                    break;
+                case GPL_PREC_TF32:
+                    st = gplk_gemm_tf32_nn((const float *)ts->dA, (const float *)ts->dB, (float *)ts->dC, n, n, n,
+                                           ts->stream);
+                    break;
+                default:
+                    st = gplk_gemm_i8_nn((const int8_t *)ts->dA, (const int8_t *)ts->dB, (int32_t *)ts->dC, n, n, n,
+                                         ts->stream);
+                    break;
+            }
+            if (st != GPLK_STATUS_OK) return -1;
+        }
+        return 0;
+    }
     static const float f1 = 1.0f;
     static const double d1 = 1.0;
     static const int i1 = 1;

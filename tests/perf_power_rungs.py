@@ -33,6 +33,10 @@ RUNGS = [
     ("ref wmma mix 1:1:1", REF, ["--op", "powervirus", "--size", "8192"], {}),
     ("gplk tcgen05 fp8 tensor-only 8192", GPLK, ["--op", "powervirus", "--tensor-backend", "cublas", "--precision",
                                                  "fp8", "--size", "8192", "--mix-fma", "0", "--mix-dram", "0"], {}),
+    ("gplk tcgen05 bf16 tensor-only 8192", GPLK, ["--op", "powervirus", "--tensor-backend", "cublas", "--precision",
+                                                  "bf16", "--size", "8192", "--mix-fma", "0", "--mix-dram", "0"], {}),
+    ("gplk tcgen05 int8 tensor-only 8192", GPLK, ["--op", "powervirus", "--tensor-backend", "cublas", "--precision",
+                                                  "int8", "--size", "8192", "--mix-fma", "0", "--mix-dram", "0"], {}),
     ("gplk tcgen05 nvfp4 tensor-only 16384", GPLK, ["--op", "powervirus", "--tensor-backend", "cublas",
                                                     "--precision", "fp4", "--size", "16384", "--mix-fma", "0",
                                                     "--mix-dram", "0"], {}),
@@ -89,9 +93,13 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--steady", type=float, default=10.0)
     ap.add_argument("--warmup", type=float, default=3.0)
+    ap.add_argument("--only", default="", help="run only rungs whose label contains this text (comma-separated)")
     args = ap.parse_args()
+    keep = [k for k in args.only.split(",") if k]
     out = {}
     for label, binary, rung_args, env in RUNGS:
+        if keep and not any(k in label for k in keep):
+            continue
         out[label] = run(binary, rung_args, args.warmup, args.steady, env)
         print(label, json.dumps(out[label]), flush=True)
     print(json.dumps(out, indent=1))

@@ -89,10 +89,11 @@ def test_powervirus_default_mix(tmp_path):
 
 
 @needs_runner
-@pytest.mark.parametrize("prec", ["fp8", "fp4"])
+@pytest.mark.parametrize("prec", ["fp8", "fp4", "bf16", "int8"])
 def test_powervirus_tensor_stream_narrow_formats(prec, tmp_path):
-    """--tensor-backend cublas with fp8/fp4: GEMMs on a concurrent stream through
-    the drop-in gpl_lt_* (libgplk tcgen05). Tensor-only, so FLOPs are counted."""
+    """--tensor-backend cublas: GEMMs on a concurrent stream through libgplk's
+    tcgen05 GEMMs (gpl_lt_* for fp8/fp4, the NN kernels for bf16/int8).
+    Tensor-only, so FLOPs are counted."""
     res, s, _ = run_rung(GPLK_RUNNER, tmp_path, "--op", "powervirus", "--tensor-backend", "cublas",
                          "--precision", prec, "--size", "8192", "--mix-fma", "0", "--mix-dram", "0")
     _ok(res, s)

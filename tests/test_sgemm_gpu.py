@@ -85,3 +85,29 @@ def test_sgemm_matches_cublas_fp32(gplk, oracle, cuda):
     torch.cuda.synchronize()
     rel = (torch.linalg.norm((C - ref).double()) / torch.linalg.norm(ref.double())).item()
     assert rel <= TOL
+
+
+def test_sgemm_matches_reference_rung_call(gplk, oracle, cuda):
+    """The reference rung's own call: cublasGemmEx COMPUTE_32F, DEFAULT_MATH,
+    column-major NN (runner/src/workload_gemm.c:155-163, built from that file
+    into the reference library). Column-major C = A * B is the row-major
+    product C^T = B^T A^T, so the row-major gplk SGEMM of (B, A) gives the
+    same bytes."""
+    import ctypes
+
+    import torch
+
+    if not oracle.ref_available():
+        pytest.skip("reference library not built")
+    n = 1024
+    A = torch.from_numpy(oracle.uniform_f32(n * n, 0, -1, 1).reshape(n, n)).to(cuda)
+    B = torch.from_numpy(oracle.uniform_f32(n * n, 1, -1, 1).reshape(n, n)).to(cuda)
+    C = torch.empty(n, n, device=cuda)
+    R = torch.empty(n, n, device=cuda)
+    gplk.sgemm(B, A, C)  # row-major (B A) = column-major (A B) with these buffers
+    st = oracle.ref_lib().ref_gemm_ex(1, A.data_ptr(), B.data_ptr(), R.data_ptr(), n,
+                                      ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert st == 0
+    rel = (torch.linalg.norm((C - R).double()) / torch.linalg.norm(R.double())).item()
+    assert rel <= TOL, rel
