@@ -305,12 +305,13 @@ __global__ void __launch_bounds__(kThreads, 1) pv_kernel(const Params p) {
             tc_fence_after();
             const uint32_t taddr = sm.tmem_base + ((warp * 32u) << 16);
             const uint32_t row = warp * 32 + lane;
-            for (int c = 0; c < 8; ++c) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(taddr + 32u * c, r);
+            // 16 columns per load: the kernel's 64-register budget (1024 threads) holds no more
+            for (int c = 0; c < 16; ++c) {
+                uint32_t r[16];
+                tmem_ld_32x32b_x16(taddr + 16u * c, r);
                 tmem_ld_wait();
 #pragma unroll
-                for (int j = 0; j < 32; ++j) p.mma_out[(size_t)row * 256 + c * 32 + j] = __uint_as_float(r[j]);
+                for (int j = 0; j < 16; ++j) p.mma_out[(size_t)row * 256 + c * 16 + j] = __uint_as_float(r[j]);
             }
         }
         tc_fence_before();
