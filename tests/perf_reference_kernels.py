@@ -16,6 +16,9 @@ prints one JSON object (not collected by pytest; run on a GPU):
              runner/src/workload_gemm.c (oracle/ref_gemm_shim.c) vs
              gplk_gemm_{bf16,f16,tf32,i8}_nn, 8192^3, identical operands:
              random values and the rung's own 0x3c byte fill
+  nn_ref_calls  four reference cublasGemmEx calls each for BF16 and TF32 at
+             8192^3 on random operands and nothing else timed: the launch
+             list to put under ncu for the library kernels' DRAM traffic
 """
 from __future__ import annotations
 
@@ -258,6 +261,21 @@ def nn(out):
             torch.cuda.empty_cache()
         res[prec] = r
     out["nn_8192_TFLOPs"] = res
+
+
+def nn_ref_calls(out):
+    n = 8192
+    L = oracle.ref_lib()
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for prec, code, dt in (("bf16", 4, torch.bfloat16), ("tf32", 2, torch.float32)):
+        A = (torch.rand(n, n, device="cuda") * 2 - 1).to(dt)
+        B = (torch.rand(n, n, device="cuda") * 2 - 1).to(dt)
+        D = torch.empty(n, n, dtype=dt, device="cuda")
+        torch.cuda.synchronize()
+        out[f"nn_ref_calls_{prec}"] = [L.ref_gemm_ex(code, A.data_ptr(), B.data_ptr(), D.data_ptr(), n, st)
+                                       for _ in range(4)]
+        torch.cuda.synchronize()
+        del A, B, D
 
 
 if __name__ == "__main__":
