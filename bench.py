@@ -42,8 +42,10 @@ NCU_TRAFFIC = {
     "memstream_vec4": 12.58e9,  # profiles/memstream_triad_2p30.md: 8 x 1.573 GB (3 x 2^27 capture)
     "memstream_bulk": 12.58e9,  # profiles/memstream_triad_2p30.md: 8 x 1.572 GB (3 x 2^27 capture)
     "sgemm": 8.4e6,             # profiles/sgemm_f32_1024.md
-    "fp8": 361.7e6,             # profiles/gemm_fp8_8192.md
+    "fp8": 339.8e6,             # profiles/gemm_fp8_8192.md (odd raster groups walking N backwards)
     "nvfp4": 1343.6e6,          # profiles/gemm_nvfp4_16384.md
+    "bf16": 1149.9e6,           # profiles/gemm_nn_bf16_i8_8192.md
+    "tf32": 2452.5e6,           # profiles/gemm_nn_bf16_i8_8192.md
 }
 
 NOMINAL_TFLOPS = {"fp8": 4500.0, "nvfp4": 9000.0, "sgemm": 148 * 128 * 2 * 1.965e9 / 1e12,
