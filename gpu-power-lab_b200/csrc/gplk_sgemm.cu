@@ -8,6 +8,9 @@
 // registers while the current one is multiplied.
 // Each output is one FP32 FFMA chain over k = 0..K-1 in order, so the result
 // differs from a double-accumulated host loop only by FP32 rounding.
+#include <mutex>
+#include <vector>
+
 #include "gplk_ptx.cuh"
 
 namespace gplk {
@@ -408,8 +411,8 @@ static int launch_split2(const float* A, const float* B, float* C, int M, int N,
 // K-major in shared memory (one 128-bit load = four k of one row), B stays
 // N-major. The FFMAs issue as Blackwell's paired FP32 FMA (__ffma2_rn: two
 // independent, individually rounded fmaf per instruction) on column pairs,
-// halving the FMA issue slots. Each output is still one FMA chain over k in
-// order. SPLIT: 2-CTA cluster split-K with a distributed-shared-memory sum.
+// halving the FMA issue slots. Each output is one FMA chain over k in order
+// (or, under stream-K below, a fixed-order sum of a few such chains).
 constexpr int kV2BM = 128, kV2BN = 128, kV2BK = 16, kV2Stages = 3, kV2Threads = 256;
 constexpr int kV2APitch = kV2BK + 4;   // floats per A row in shared memory (80 B)
 constexpr int kV2AStage = kV2BM * kV2APitch;
@@ -424,54 +427,75 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-template <bool SPLIT>
-__global__ void __launch_bounds__(kV2Threads, 1) sgemm_v2_kernel(const float* __restrict__ A, const float* __restrict__ B,
-                                                                  float* __restrict__ C, int M, int N, int K, int lda,
-                                                                  int ldb, int ldc) {
-    extern __shared__ __align__(16) float v2_smem[];
-    float* As = v2_smem;                          // [stage][128][kV2APitch]
-    float* Bs = v2_smem + kV2Stages * kV2AStage;  // [stage][16][128]
+// acc += the 128 x 16 A slab x the 16 x 128 B slab of one ring stage.
+__device__ __forceinline__ void v2_ktile(const float* as, const float* bs, int tx, int ty, float2 (&acc)[8][4]) {
+#pragma unroll
+    for (int kq = 0; kq < kV2BK; kq += 4) {
+        float4 af[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int row = (i >> 2) * 64 + ty * 4 + (i & 3);
+            af[i] = *reinterpret_cast<const float4*>(as + row * kV2APitch + kq);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+            const float4 b0 = *reinterpret_cast<const float4*>(bs + (kq + kk) * kV2BN + tx * 4);
+            const float4 b1 = *reinterpret_cast<const float4*>(bs + (kq + kk) * kV2BN + 64 + tx * 4);
+            const float2 bp[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w), make_float2(b1.x, b1.y),
+                                  make_float2(b1.z, b1.w)};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float av = kk == 0 ? af[i].x : kk == 1 ? af[i].y : kk == 2 ? af[i].z : af[i].w;
+                const float2 a2 = make_float2(av, av);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = __ffma2_rn(a2, bp[j], acc[i][j]);
+            }
+        }
+    }
+}
+
+// Copies one 16-wide K step of the 128 x 128 tile at (m0, n0) into a ring
+// stage: each thread 2 A chunks (row r, k-quad q) and 2 B chunks; rows,
+// columns and k past the matrix are zero-filled.
+__device__ __forceinline__ void v2_issue(const float* __restrict__ A, const float* __restrict__ B, int M, int N,
+                                         int lda, int ldb, int m0, int n0, int k0, int k_end, float* as,
+                                         float* bs) {
+    const int tid = threadIdx.x;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int idx = tid + i * kV2Threads;  // 0..511
+        const int r = idx >> 2, q = idx & 3;
+        const int gm = m0 + r, gk = k0 + q * 4;
+        const bool ok = gm < M && gk < k_end;
+        cp_async16(as + r * kV2APitch + q * 4, ok ? A + (size_t)gm * lda + gk : A, ok);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int idx = tid + i * kV2Threads;
+        const int r = idx >> 5, c4 = idx & 31;
+        const int gk = k0 + r, gn = n0 + c4 * 4;
+        const bool ok = gk < k_end && gn < N;
+        cp_async16(bs + r * kV2BN + c4 * 4, ok ? B + (size_t)gk * ldb + gn : B, ok);
+    }
+}
+
+// The pipelined main loop: acc += A[m0.., k_begin..k_end) x B[k_begin..k_end, n0..]
+// for one 128 x 128 tile, through the 3-stage cp.async ring in `smem`. On
+// return every copy has landed and the block has synchronised, so the ring
+// may be refilled for another tile.
+__device__ __forceinline__ void v2_mainloop(const float* __restrict__ A, const float* __restrict__ B, int M, int N,
+                                            int lda, int ldb, int m0, int n0, int k_begin, int k_end,
+                                            float* smem, float2 (&acc)[8][4]) {
+    float* As = smem;                          // [stage][128][kV2APitch]
+    float* Bs = smem + kV2Stages * kV2AStage;  // [stage][16][128]
     const int tid = threadIdx.x;
     const int tx = tid % 16, ty = tid / 16;
-    const int m0 = blockIdx.y * kV2BM;
-    const uint32_t rank = SPLIT ? cluster_ctarank() : 0u;
-    const int n0 = (SPLIT ? (blockIdx.x >> 1) : blockIdx.x) * kV2BN;
-    int k_begin = 0, k_end = K;
-    if (SPLIT) {
-        const int k_half = ((K + 2 * kV2BK - 1) / (2 * kV2BK)) * kV2BK;
-        k_begin = rank == 0 ? 0 : k_half;
-        k_end = rank == 0 ? min(K, k_half) : K;
-    }
     const int ktiles = k_end > k_begin ? (k_end - k_begin + kV2BK - 1) / kV2BK : 0;
-
-    // Each thread copies 2 A chunks (row r, k-quad q) and 2 B chunks.
     auto issue = [&](int kt) {
         const int st = kt % kV2Stages;
-        const int k0 = k_begin + kt * kV2BK;
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const int idx = tid + i * kV2Threads;  // 0..511
-            const int r = idx >> 2, q = idx & 3;
-            const int gm = m0 + r, gk = k0 + q * 4;
-            const bool ok = gm < M && gk < k_end;
-            cp_async16(As + st * kV2AStage + r * kV2APitch + q * 4, ok ? A + (size_t)gm * lda + gk : A, ok);
-        }
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const int idx = tid + i * kV2Threads;
-            const int r = idx >> 5, c4 = idx & 31;
-            const int gk = k0 + r, gn = n0 + c4 * 4;
-            const bool ok = gk < k_end && gn < N;
-            cp_async16(Bs + st * kV2BStage + r * kV2BN + c4 * 4, ok ? B + (size_t)gk * ldb + gn : B, ok);
-        }
+        v2_issue(A, B, M, N, lda, ldb, m0, n0, k_begin + kt * kV2BK, k_end, As + st * kV2AStage,
+                 Bs + st * kV2BStage);
     };
-
-    float2 acc[8][4];  // acc[row][column pair]
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = make_float2(0.f, 0.f);
-
 #pragma unroll
     for (int s = 0; s < kV2Stages - 1; ++s) {
         if (s < ktiles) issue(s);
@@ -482,63 +506,18 @@ __global__ void __launch_bounds__(kV2Threads, 1) sgemm_v2_kernel(const float* __
         __syncthreads();
         if (kt + kV2Stages - 1 < ktiles) issue(kt + kV2Stages - 1);
         cp_async_commit();
-        const float* as = As + (kt % kV2Stages) * kV2AStage;
-        const float* bs = Bs + (kt % kV2Stages) * kV2BStage;
-#pragma unroll
-        for (int kq = 0; kq < kV2BK; kq += 4) {
-            float4 af[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int row = (i >> 2) * 64 + ty * 4 + (i & 3);
-                af[i] = *reinterpret_cast<const float4*>(as + row * kV2APitch + kq);
-            }
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-                const float4 b0 = *reinterpret_cast<const float4*>(bs + (kq + kk) * kV2BN + tx * 4);
-                const float4 b1 = *reinterpret_cast<const float4*>(bs + (kq + kk) * kV2BN + 64 + tx * 4);
-                const float2 bp[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w), make_float2(b1.x, b1.y),
-                                      make_float2(b1.z, b1.w)};
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const float av = kk == 0 ? af[i].x : kk == 1 ? af[i].y : kk == 2 ? af[i].z : af[i].w;
-                    const float2 a2 = make_float2(av, av);
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) acc[i][j] = __ffma2_rn(a2, bp[j], acc[i][j]);
-                }
-            }
-        }
+        v2_ktile(As + (kt % kV2Stages) * kV2AStage, Bs + (kt % kV2Stages) * kV2BStage, tx, ty, acc);
     }
     cp_async_wait<0>();
     __syncthreads();
+}
 
-    if (SPLIT) {
-        // CTA 1 hands its partial tile to CTA 0 through distributed shared
-        // memory ([v][thread] float4 layout, contiguous per warp).
-        // The receive buffer has its own region after the operand ring, so
-        // CTA 1 may write it while CTA 0 still reads its last stage.
-        float4* recv = reinterpret_cast<float4*>(v2_smem + kV2Stages * (kV2AStage + kV2BStage));
-        if (rank == 1) {
-            const uint32_t dst0 = mapa_shared(smem_u32(recv), 0);
-#pragma unroll
-            for (int v = 0; v < 16; ++v) {
-                const int i = v >> 1, j = (v & 1) * 2;
-                const uint32_t addr = dst0 + (uint32_t)((v * kV2Threads + tid) * 16);
-                asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(acc[i][j].x),
-                             "f"(acc[i][j].y), "f"(acc[i][j + 1].x), "f"(acc[i][j + 1].y)
-                             : "memory");
-            }
-        }
-        cluster_sync();
-        if (rank == 1) return;
-#pragma unroll
-        for (int v = 0; v < 16; ++v) {
-            const int i = v >> 1, j = (v & 1) * 2;
-            const float4 q = recv[v * kV2Threads + tid];
-            acc[i][j] = __fadd2_rn(acc[i][j], make_float2(q.x, q.y));
-            acc[i][j + 1] = __fadd2_rn(acc[i][j + 1], make_float2(q.z, q.w));
-        }
-    }
-
+// Stores the tile's accumulators (rows ty*4+i and 64+ty*4+i, column pairs
+// tx*4.. and 64+tx*4..) with bounds checks.
+__device__ __forceinline__ void v2_store(float* __restrict__ C, int M, int N, int ldc, int m0, int n0,
+                                         const float2 (&acc)[8][4]) {
+    const int tid = threadIdx.x;
+    const int tx = tid % 16, ty = tid / 16;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const int gm = m0 + (i >> 2) * 64 + ty * 4 + (i & 3);
@@ -560,39 +539,213 @@ __global__ void __launch_bounds__(kV2Threads, 1) sgemm_v2_kernel(const float* __
     }
 }
 
-template <bool SPLIT>
+__global__ void __launch_bounds__(kV2Threads, 1) sgemm_v2_kernel(const float* __restrict__ A, const float* __restrict__ B,
+                                                                  float* __restrict__ C, int M, int N, int K, int lda,
+                                                                  int ldb, int ldc) {
+    extern __shared__ __align__(16) float v2_smem[];
+    const int m0 = blockIdx.y * kV2BM, n0 = blockIdx.x * kV2BN;
+    float2 acc[8][4];  // acc[row][column pair]
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = make_float2(0.f, 0.f);
+    v2_mainloop(A, B, M, N, lda, ldb, m0, n0, 0, K, v2_smem, acc);
+    v2_store(C, M, N, ldc, m0, n0, acc);
+}
+
+// ------------------------------------------------------------ stream-K
+// When the 128 x 128 tiles do not fill whole waves of the GPU, one CTA per SM
+// takes an equal share of the (tile, 16-wide K step) units, in order: its
+// share starts with the tail of one tile's K range, continues with whole
+// tiles and ends with the head of another. A tile split between CTAs is
+// finished by the CTA holding its K = 0 head (the "owner", which reaches it
+// last): the others each park their partial sums in a per-CTA slot of a
+// global workspace (64 KiB, [v][thread] float4) and raise their flag; the
+// owner waits for each flag (bounded), adds the partials in CTA order and
+// stores C. Each CTA has at most one such parked partial (its first
+// segment), and owners only wait on higher-numbered CTAs, so with every CTA
+// resident (cooperative launch) the waits always end. Deterministic: the
+// summation order depends only on M, N, K and the SM count. A flag holds
+// the launch's epoch (so a flag left raised by a launch that timed out is
+// not mistaken for a fresh one), and the owner clears each flag it consumed
+// (so a replayed CUDA graph, whose epoch is frozen, also starts clean).
+__device__ __forceinline__ void st_release_gpu(unsigned* p, unsigned v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__global__ void __launch_bounds__(kV2Threads, 1)
+    sgemm_sk_kernel(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C, int M, int N,
+                    int K, int lda, int ldb, int ldc, float4* __restrict__ ws, unsigned* __restrict__ flags,
+                    unsigned epoch) {
+    extern __shared__ __align__(16) float v2_smem[];
+    __shared__ int s_ok;
+    const int tid = threadIdx.x;
+    const int nt = (N + kV2BN - 1) / kV2BN, mt = (M + kV2BM - 1) / kV2BM;
+    const int iters = (K + kV2BK - 1) / kV2BK;  // K steps per tile
+    const long long U = (long long)mt * nt * iters;
+    const int G = (int)gridDim.x, c = (int)blockIdx.x;
+    auto share_begin = [&](int q) { return U * q / G; };
+    long long u = share_begin(c);
+    const long long u_end = share_begin(c + 1);
+    while (u < u_end) {
+        const int t = (int)(u / iters);
+        const long long tile_u0 = (long long)t * iters;
+        const int kb = (int)(u - tile_u0);
+        const int ke = (int)min((long long)iters, u_end - tile_u0);
+        const int m0 = (t / nt) * kV2BM, n0 = (t % nt) * kV2BN;
+        float2 acc[8][4];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[i][j] = make_float2(0.f, 0.f);
+        v2_mainloop(A, B, M, N, lda, ldb, m0, n0, kb * kV2BK, min(K, ke * kV2BK), v2_smem, acc);
+        if (kb != 0) {
+            // Not the owner: park the partial tile, then raise the flag.
+            float4* dst = ws + (size_t)c * (16 * kV2Threads);
+#pragma unroll
+            for (int v = 0; v < 16; ++v) {
+                const int i = v >> 1, j = (v & 1) * 2;
+                __stcg(dst + v * kV2Threads + tid,
+                       make_float4(acc[i][j].x, acc[i][j].y, acc[i][j + 1].x, acc[i][j + 1].y));
+            }
+            __syncthreads();
+            if (tid == 0) {
+                __threadfence();
+                st_release_gpu(flags + c, epoch);
+            }
+        } else {
+            if (ke < iters) {
+                // Owner of a split tile: add the partials of the CTAs whose
+                // shares start inside this tile, in CTA order.
+                const long long tile_u1 = tile_u0 + iters;
+                for (int q = c + 1; q < G; ++q) {
+                    const long long qb = share_begin(q), qe = share_begin(q + 1);
+                    if (qb >= tile_u1) break;
+                    if (qb == qe) continue;  // empty share: nothing parked
+                    if (tid == 0) {
+                        bool ok = ld_acquire_gpu(flags + q) == epoch;
+                        if (!ok) {
+                            const uint64_t t0 = globaltimer_ns();
+                            uint32_t spins = 0;
+                            while (!(ok = ld_acquire_gpu(flags + q) == epoch)) {
+                                if ((++spins & 63u) == 0 && globaltimer_ns() - t0 > kWaitBudgetNs) {
+                                    record_error(GPLK_STATUS_DEVICE_TIMEOUT, 0x0B01);
+                                    break;
+                                }
+                            }
+                        }
+                        if (ok) flags[q] = 0u;  // consumed; nothing else touches it in this launch
+                        s_ok = ok;
+                    }
+                    __syncthreads();
+                    if (s_ok) {
+                        const float4* src = ws + (size_t)q * (16 * kV2Threads);
+#pragma unroll
+                        for (int v = 0; v < 16; ++v) {
+                            const int i = v >> 1, j = (v & 1) * 2;
+                            const float4 p4 = __ldcg(src + v * kV2Threads + tid);
+                            acc[i][j] = __fadd2_rn(acc[i][j], make_float2(p4.x, p4.y));
+                            acc[i][j + 1] = __fadd2_rn(acc[i][j + 1], make_float2(p4.z, p4.w));
+                        }
+                    }
+                    __syncthreads();  // s_ok is rewritten for the next contributor
+                    if (qe >= tile_u1) break;
+                }
+            }
+            v2_store(C, M, N, ldc, m0, n0, acc);
+        }
+        u = tile_u0 + ke;
+    }
+}
+
 static int launch_v2(const float* A, const float* B, float* C, int M, int N, int K, int lda, int ldb, int ldc,
                      cudaStream_t stream) {
-    int smem = (int)(sizeof(float) * kV2Stages * (kV2AStage + kV2BStage));
-    if (SPLIT) smem += (int)(16 * kV2Threads * sizeof(float4));
+    const int smem = (int)(sizeof(float) * kV2Stages * (kV2AStage + kV2BStage));
     static thread_local uint64_t configured = 0;
     int dev = 0;
     cudaGetDevice(&dev);
     if (!(configured & (1ull << dev))) {
-        if (cudaFuncSetAttribute(sgemm_v2_kernel<SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-            cudaSuccess)
+        if (cudaFuncSetAttribute(sgemm_v2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
             return GPLK_STATUS_LAUNCH_FAIL;
         configured |= 1ull << dev;
     }
     const int nt = (N + kV2BN - 1) / kV2BN, mt = (M + kV2BM - 1) / kV2BM;
-    if (!SPLIT) {
-        sgemm_v2_kernel<false><<<dim3(nt, mt), kV2Threads, smem, stream>>>(A, B, C, M, N, K, lda, ldb, ldc);
-    } else {  // clusters of two along x, set at launch
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(2 * nt, mt, 1);
-        cfg.blockDim = dim3(kV2Threads, 1, 1);
-        cfg.dynamicSmemBytes = (size_t)smem;
-        cfg.stream = stream;
-        cudaLaunchAttribute attr;
-        attr.id = cudaLaunchAttributeClusterDimension;
-        attr.val.clusterDim.x = 2;
-        attr.val.clusterDim.y = 1;
-        attr.val.clusterDim.z = 1;
-        cfg.attrs = &attr;
-        cfg.numAttrs = 1;
-        if (cudaLaunchKernelEx(&cfg, sgemm_v2_kernel<true>, A, B, C, M, N, K, lda, ldb, ldc) != cudaSuccess)
+    sgemm_v2_kernel<<<dim3(nt, mt), kV2Threads, smem, stream>>>(A, B, C, M, N, K, lda, ldb, ldc);
+    return launch_status(cudaGetLastError());
+}
+
+// One stream-K workspace per (device, stream): partial-tile slots and flags
+// for one CTA per SM. Concurrent GEMMs on different streams never share one;
+// GEMMs on one stream are ordered by the stream. Allocated on first use
+// (cudaMalloc, so the first call for a stream must not be inside a CUDA
+// graph capture) and kept for the life of the process.
+struct SkSlot {
+    int device;
+    cudaStream_t stream;
+    int ctas;
+    float4* ws;
+    unsigned* flags;
+    unsigned epoch;
+};
+static std::mutex g_sk_mu;
+static std::vector<SkSlot> g_sk_slots;
+
+static int launch_sk(const float* A, const float* B, float* C, int M, int N, int K, int lda, int ldb, int ldc,
+                     int sm_count, cudaStream_t stream) {
+    const int smem = (int)(sizeof(float) * kV2Stages * (kV2AStage + kV2BStage));
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static thread_local uint64_t configured = 0;
+    if (!(configured & (1ull << dev))) {
+        if (cudaFuncSetAttribute(sgemm_sk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+            cudaSuccess)
             return GPLK_STATUS_LAUNCH_FAIL;
+        configured |= 1ull << dev;
     }
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sgemm_sk_kernel, kV2Threads, (size_t)smem) !=
+            cudaSuccess ||
+        per_sm < 1)
+        return GPLK_STATUS_UNSUPPORTED;
+    const int G = sm_count;
+    float4* ws = nullptr;
+    unsigned* flags = nullptr;
+    unsigned epoch = 0;
+    {
+        std::lock_guard<std::mutex> lock(g_sk_mu);
+        SkSlot* slot = nullptr;
+        for (SkSlot& s : g_sk_slots)
+            if (s.device == dev && s.stream == stream && s.ctas == G) slot = &s;
+        if (!slot) {
+            SkSlot s{dev, stream, G, nullptr, nullptr, 0u};
+            if (cudaMalloc(&s.ws, (size_t)G * 16 * kV2Threads * sizeof(float4)) != cudaSuccess)
+                return GPLK_STATUS_CUDA_ERROR;
+            if (cudaMalloc(&s.flags, (size_t)G * sizeof(unsigned)) != cudaSuccess) {
+                cudaFree(s.ws);
+                return GPLK_STATUS_CUDA_ERROR;
+            }
+            if (cudaMemsetAsync(s.flags, 0, (size_t)G * sizeof(unsigned), stream) != cudaSuccess) {
+                cudaFree(s.ws);
+                cudaFree(s.flags);
+                return GPLK_STATUS_LAUNCH_FAIL;
+            }
+            g_sk_slots.push_back(s);
+            slot = &g_sk_slots.back();
+        }
+        if (++slot->epoch == 0u) slot->epoch = 1u;
+        ws = slot->ws;
+        flags = slot->flags;
+        epoch = slot->epoch;
+    }
+    void* args[] = {&A, &B, &C, &M, &N, &K, &lda, &ldb, &ldc, &ws, &flags, &epoch};
+    if (cudaLaunchCooperativeKernel((const void*)sgemm_sk_kernel, dim3((unsigned)G), dim3(kV2Threads), args,
+                                    (size_t)smem, stream) != cudaSuccess)
+        return GPLK_STATUS_LAUNCH_FAIL;
     return launch_status(cudaGetLastError());
 }
 
@@ -625,16 +778,19 @@ extern "C" int gplk_sgemm_f32(const float* A, const float* B, float* C, int M, i
     if (st != GPLK_STATUS_OK) return st;
     const bool vec = aligned16(A) && aligned16(B) && aligned16(C) && (lda % 4 == 0) && (ldb % 4 == 0) &&
                      (ldc % 4 == 0) && (K % 4 == 0) && (N % 4 == 0);
-    // 128 x 128 tiles (8 x 8 per thread). When they cannot fill the GPU, a
-    // 2-CTA cluster splits K per tile (each tile then occupies two SMs); tiny
-    // or shallow problems fall back to 64 x 64 tiles.
+    // 128 x 128 tiles (8 x 8 per thread). When they leave more than a tenth
+    // of the last wave's SMs idle, stream-K spreads the K steps evenly over
+    // one CTA per SM; tiny or shallow problems fall back to 64 x 64 tiles.
     const long tiles128 = (long)((M + 127) / 128) * ((N + 127) / 128);
-    if (vec) {  // 16-byte aligned rows: the cp.async + FFMA2 kernel
-        if (tiles128 >= d.sm_count) return sgemm::launch_v2<false>(A, B, C, M, N, K, lda, ldb, ldc, stream);
-        if (K >= 256 && 2 * tiles128 >= d.sm_count / 2)
-            return sgemm::launch_v2<true>(A, B, C, M, N, K, lda, ldb, ldc, stream);
+    if (vec) {  // 16-byte aligned rows: the cp.async + FFMA2 kernels
+        const long waves = (tiles128 + d.sm_count - 1) / d.sm_count;
+        const bool ragged = tiles128 * 10 < waves * d.sm_count * 9;
+        if (K >= 256 && 4 * tiles128 >= d.sm_count && ragged) {
+            const int st = sgemm::launch_sk(A, B, C, M, N, K, lda, ldb, ldc, d.sm_count, stream);
+            if (st != GPLK_STATUS_UNSUPPORTED) return st;
+        }
         if (tiles128 * 2 >= d.sm_count / 4)
-            return sgemm::launch_v2<false>(A, B, C, M, N, K, lda, ldb, ldc, stream);
+            return sgemm::launch_v2(A, B, C, M, N, K, lda, ldb, ldc, stream);
     }
     if (tiles128 >= d.sm_count)
         return sgemm::launch<128, 128, 16, 8, 8>(A, B, C, M, N, K, lda, ldb, ldc, vec, stream);

@@ -75,7 +75,11 @@ int gplk_copy_f32(float *dst, const float *src, size_t n, cudaStream_t stream);
  * A is M x K (leading dimension lda), B is K x N (ldb), C is M x N (ldc).
  * Replaces cublasGemmEx with CUBLAS_COMPUTE_32F / CUBLAS_DEFAULT_MATH,
  * runner/src/workload_gemm.c:155-163, :174-179, :199-204 (column-major
- * C = A * B there, which is the row-major product C^T = B^T * A^T here). */
+ * C = A * B there, which is the row-major product C^T = B^T * A^T here).
+ * Problems whose 128 x 128 tiles leave a wave of SMs ragged run stream-K
+ * (a cooperative launch, one block per SM); the first such call on a stream
+ * allocates that stream's workspace (64 KiB per SM, cudaMalloc), so it must
+ * not be the first call on that stream inside a CUDA graph capture. */
 int gplk_sgemm_f32(const float *A, const float *B, float *C, int M, int N, int K, int lda,
                    int ldb, int ldc, cudaStream_t stream);
 

@@ -6,8 +6,8 @@ prints one JSON object (not collected by pytest; run on a GPU):
   memstream  stream_triad_kernel compiled from the reference source
              (runner/src/workload_memstream.cu:43-54, its launch geometry)
              vs gplk_triad_f32 / gplk_triad_f32_bulk, 3 x 2^30 FP32
-  sgemm      cuBLAS FP32 (TF32 off; the reference's cublasGemmEx
-             COMPUTE_32F) vs gplk_sgemm_f32, 1024^3
+  sgemm      the reference's cublasGemmEx FP32 rung call (COMPUTE_32F,
+             oracle/ref_gemm_shim.c) vs gplk_sgemm_f32, 1024 / 2048 / 4096
   fp8        the reference's gemm_lt.cu cuBLASLt FP8 (gpl_lt_enqueue)
              vs gplk_gemm_fp8_tn, 8192^3
   nvfp4      cuBLASLt NVFP4 with VEC16_UE4M3 scales (oracle/lt_nvfp4.cu)
@@ -136,16 +136,27 @@ def memstream(out):
 
 
 def sgemm(out):
+    """The reference rung's cublasGemmEx FP32 call (oracle/ref_gemm_shim.c)
+    against gplk_sgemm_f32 at 1024 (the parity case), 2048 (ragged waves of
+    128 x 128 tiles: stream-K) and 4096 (the rung's default --size)."""
     torch.backends.cuda.matmul.allow_tf32 = False
-    n = 1024
-    A = torch.rand(n, n, device="cuda") * 2 - 1
-    B = torch.rand(n, n, device="cuda") * 2 - 1
-    C = torch.empty(n, n, device="cuda")
-    tf = lambda ms: 2 * n ** 3 / (ms / 1e3) / 1e12
-    out["sgemm_1024_TFLOPs"] = {
-        "cublas_fp32": tf(sustained(lambda: torch.matmul(A, B, out=C))[0]),
-        "gplk_sgemm": tf(sustained(lambda: gplk.sgemm(A, B, C))[0]),
-    }
+    L = oracle.ref_lib()
+    st = lambda: ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    res = {}
+    for n in (1024, 2048, 4096):
+        A = torch.rand(n, n, device="cuda") * 2 - 1
+        B = torch.rand(n, n, device="cuda") * 2 - 1
+        C = torch.empty(n, n, device="cuda")
+        R = torch.empty(n, n, device="cuda")
+        tf = lambda ms: round(2 * n ** 3 / (ms / 1e3) / 1e12, 2)
+        case = {}
+        for name, fn in (("reference_cublasGemmEx_fp32",
+                          lambda: L.ref_gemm_ex(1, A.data_ptr(), B.data_ptr(), R.data_ptr(), n, st())),
+                         ("gplk_sgemm", lambda: gplk.sgemm(A, B, C))):
+            ms, mhz, w = sustained(fn)
+            case[name] = {"tflops": tf(ms), "sm_mhz": mhz, "watts": w}
+        res[n] = case
+    out["sgemm_TFLOPs"] = res
 
 
 def fp8(out):

@@ -111,3 +111,35 @@ def test_sgemm_matches_reference_rung_call(gplk, oracle, cuda):
     assert st == 0
     rel = (torch.linalg.norm((C - R).double()) / torch.linalg.norm(R.double())).item()
     assert rel <= TOL, rel
+
+
+def test_sgemm_stream_k_repeatable_and_per_stream(gplk, oracle, cuda):
+    """Shapes whose 128 x 128 tiles leave the last wave ragged run stream-K
+    (partial tiles parked in a per-stream workspace, flags carrying a launch
+    epoch). Back-to-back calls with new inputs, and calls on two streams at
+    once, must each be exact to the tolerance and bit-identical run to run."""
+    import torch
+
+    M, N, K = 2048, 2048, 2048  # 256 tiles on 148 SMs: stream-K
+    gplk.status_read()  # start from a clear device status word
+    ins = [(oracle.uniform_f32(M * K, seed=20 + i, lo=-1.0, hi=1.0).reshape(M, K),
+            oracle.uniform_f32(K * N, seed=40 + i, lo=-1.0, hi=1.0).reshape(K, N)) for i in range(2)]
+    want = [oracle.sgemm_f64acc(A, B) for A, B in ins]
+    dev = [(torch.from_numpy(A).to(cuda), torch.from_numpy(B).to(cuda)) for A, B in ins]
+    outs = [torch.full((M, N), float("nan"), device=cuda) for _ in range(4)]
+    for r in range(2):  # same stream: first operand pair, second, first again
+        gplk.sgemm(dev[0][0], dev[0][1], outs[0])
+        gplk.sgemm(dev[1][0], dev[1][1], outs[1])
+        gplk.sgemm(dev[0][0], dev[0][1], outs[2])
+    torch.cuda.synchronize()
+    s1, s2 = torch.cuda.Stream(device=cuda), torch.cuda.Stream(device=cuda)
+    with torch.cuda.stream(s1):
+        gplk.sgemm(dev[0][0], dev[0][1], outs[3], stream=s1)
+    with torch.cuda.stream(s2):
+        gplk.sgemm(dev[1][0], dev[1][1], outs[1], stream=s2)
+    torch.cuda.synchronize()
+    got = [o.cpu().numpy() for o in outs]
+    assert _rel_fro(got[0], want[0]) <= TOL
+    assert _rel_fro(got[1], want[1]) <= TOL
+    assert np.array_equal(got[0], got[2]) and np.array_equal(got[0], got[3])
+    assert gplk.status_read() == (0, 0)
