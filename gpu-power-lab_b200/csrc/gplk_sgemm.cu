@@ -413,7 +413,23 @@ static int launch_split2(const float* A, const float* B, float* C, int M, int N,
 // independent, individually rounded fmaf per instruction) on column pairs,
 // halving the FMA issue slots. Each output is one FMA chain over k in order
 // (or, under stream-K below, a fixed-order sum of a few such chains).
-constexpr int kV2BM = 128, kV2BN = 128, kV2BK = 16, kV2Stages = 3, kV2Threads = 256;
+constexpr int kV2BM = 128, kV2BN = 128, kV2BK = 16, kV2Stages = 3;
+// Thread layout for TN outputs per thread along N (each thread: 8 rows x TN
+// columns, in two 64-column halves).
+template <int TN>
+struct V2T {
+    static constexpr int GW = TN / 2;           // columns per thread in each 64-column half
+    static constexpr int NP = TN / 2;           // column pairs per thread
+    static constexpr int TX = kV2BN / TN;       // threads along N
+    static constexpr int Threads = TX * 16;     // 16 threads along M
+    static constexpr int Park = 2 * TN;         // float4 per thread in a parked partial tile
+};
+// Whole-wave grids use 8 x 16 per thread (128 threads, two blocks per SM):
+// 4096^3 measured 54.4 TFLOP/s against 50.3 with 8 x 8 (256 threads).
+// Stream-K keeps 8 x 8: its extra state spills at 8 x 16, and with one
+// block per SM 8 x 16 measured slower there (1024^3: 33.9 against 36.6).
+constexpr int kV2TNDense = 16;
+constexpr int kV2TNStreamK = 8;
 constexpr int kV2APitch = kV2BK + 4;   // floats per A row in shared memory (80 B)
 constexpr int kV2AStage = kV2BM * kV2APitch;
 constexpr int kV2BStage = kV2BK * kV2BN;
@@ -428,7 +444,10 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // acc += the 128 x 16 A slab x the 16 x 128 B slab of one ring stage.
-__device__ __forceinline__ void v2_ktile(const float* as, const float* bs, int tx, int ty, float2 (&acc)[8][4]) {
+template <int TN>
+__device__ __forceinline__ void v2_ktile(const float* as, const float* bs, int tx, int ty,
+                                         float2 (&acc)[8][TN / 2]) {
+    using T = V2T<TN>;
 #pragma unroll
     for (int kq = 0; kq < kV2BK; kq += 4) {
         float4 af[8];
@@ -439,39 +458,52 @@ __device__ __forceinline__ void v2_ktile(const float* as, const float* bs, int t
         }
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-            const float4 b0 = *reinterpret_cast<const float4*>(bs + (kq + kk) * kV2BN + tx * 4);
-            const float4 b1 = *reinterpret_cast<const float4*>(bs + (kq + kk) * kV2BN + 64 + tx * 4);
-            const float2 bp[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w), make_float2(b1.x, b1.y),
-                                  make_float2(b1.z, b1.w)};
+            float2 bp[T::NP];
+#pragma unroll
+            for (int g = 0; g < 2; ++g) {
+                const float* src = bs + (kq + kk) * kV2BN + g * 64 + tx * T::GW;
+                if constexpr (T::GW % 4 == 0) {
+#pragma unroll
+                    for (int h = 0; h < T::GW / 4; ++h) {
+                        const float4 b = *reinterpret_cast<const float4*>(src + 4 * h);
+                        bp[g * (T::GW / 2) + 2 * h] = make_float2(b.x, b.y);
+                        bp[g * (T::GW / 2) + 2 * h + 1] = make_float2(b.z, b.w);
+                    }
+                } else {
+                    bp[g] = *reinterpret_cast<const float2*>(src);
+                }
+            }
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 const float av = kk == 0 ? af[i].x : kk == 1 ? af[i].y : kk == 2 ? af[i].z : af[i].w;
                 const float2 a2 = make_float2(av, av);
 #pragma unroll
-                for (int j = 0; j < 4; ++j) acc[i][j] = __ffma2_rn(a2, bp[j], acc[i][j]);
+                for (int j = 0; j < T::NP; ++j) acc[i][j] = __ffma2_rn(a2, bp[j], acc[i][j]);
             }
         }
     }
 }
 
 // Copies one 16-wide K step of the 128 x 128 tile at (m0, n0) into a ring
-// stage: each thread 2 A chunks (row r, k-quad q) and 2 B chunks; rows,
-// columns and k past the matrix are zero-filled.
+// stage: 512 16-byte chunks of A (row r, k-quad q) and 512 of B spread over
+// the threads; rows, columns and k past the matrix are zero-filled.
+template <int TN>
 __device__ __forceinline__ void v2_issue(const float* __restrict__ A, const float* __restrict__ B, int M, int N,
                                          int lda, int ldb, int m0, int n0, int k0, int k_end, float* as,
                                          float* bs) {
+    constexpr int kThreads = V2T<TN>::Threads;
     const int tid = threadIdx.x;
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        const int idx = tid + i * kV2Threads;  // 0..511
+    for (int i = 0; i < 512 / kThreads; ++i) {
+        const int idx = tid + i * kThreads;  // 0..511
         const int r = idx >> 2, q = idx & 3;
         const int gm = m0 + r, gk = k0 + q * 4;
         const bool ok = gm < M && gk < k_end;
         cp_async16(as + r * kV2APitch + q * 4, ok ? A + (size_t)gm * lda + gk : A, ok);
     }
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        const int idx = tid + i * kV2Threads;
+    for (int i = 0; i < 512 / kThreads; ++i) {
+        const int idx = tid + i * kThreads;
         const int r = idx >> 5, c4 = idx & 31;
         const int gk = k0 + r, gn = n0 + c4 * 4;
         const bool ok = gk < k_end && gn < N;
@@ -483,17 +515,19 @@ __device__ __forceinline__ void v2_issue(const float* __restrict__ A, const floa
 // for one 128 x 128 tile, through the 3-stage cp.async ring in `smem`. On
 // return every copy has landed and the block has synchronised, so the ring
 // may be refilled for another tile.
+template <int TN>
 __device__ __forceinline__ void v2_mainloop(const float* __restrict__ A, const float* __restrict__ B, int M, int N,
                                             int lda, int ldb, int m0, int n0, int k_begin, int k_end,
-                                            float* smem, float2 (&acc)[8][4]) {
+                                            float* smem, float2 (&acc)[8][TN / 2]) {
+    using T = V2T<TN>;
     float* As = smem;                          // [stage][128][kV2APitch]
     float* Bs = smem + kV2Stages * kV2AStage;  // [stage][16][128]
     const int tid = threadIdx.x;
-    const int tx = tid % 16, ty = tid / 16;
+    const int tx = tid % T::TX, ty = tid / T::TX;
     const int ktiles = k_end > k_begin ? (k_end - k_begin + kV2BK - 1) / kV2BK : 0;
     auto issue = [&](int kt) {
         const int st = kt % kV2Stages;
-        v2_issue(A, B, M, N, lda, ldb, m0, n0, k_begin + kt * kV2BK, k_end, As + st * kV2AStage,
+        v2_issue<TN>(A, B, M, N, lda, ldb, m0, n0, k_begin + kt * kV2BK, k_end, As + st * kV2AStage,
                  Bs + st * kV2BStage);
     };
 #pragma unroll
@@ -506,51 +540,59 @@ __device__ __forceinline__ void v2_mainloop(const float* __restrict__ A, const f
         __syncthreads();
         if (kt + kV2Stages - 1 < ktiles) issue(kt + kV2Stages - 1);
         cp_async_commit();
-        v2_ktile(As + (kt % kV2Stages) * kV2AStage, Bs + (kt % kV2Stages) * kV2BStage, tx, ty, acc);
+        v2_ktile<TN>(As + (kt % kV2Stages) * kV2AStage, Bs + (kt % kV2Stages) * kV2BStage, tx, ty, acc);
     }
     cp_async_wait<0>();
     __syncthreads();
 }
 
-// Stores the tile's accumulators (rows ty*4+i and 64+ty*4+i, column pairs
-// tx*4.. and 64+tx*4..) with bounds checks.
+// Stores the tile's accumulators (rows ty*4+i and 64+ty*4+i, columns
+// tx*T::GW.. and 64+tx*T::GW..) with bounds checks.
+template <int TN>
 __device__ __forceinline__ void v2_store(float* __restrict__ C, int M, int N, int ldc, int m0, int n0,
-                                         const float2 (&acc)[8][4]) {
+                                         const float2 (&acc)[8][TN / 2]) {
+    using T = V2T<TN>;
     const int tid = threadIdx.x;
-    const int tx = tid % 16, ty = tid / 16;
+    const int tx = tid % T::TX, ty = tid / T::TX;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const int gm = m0 + (i >> 2) * 64 + ty * 4 + (i & 3);
         if (gm >= M) continue;
 #pragma unroll
         for (int g = 0; g < 2; ++g) {
-            const int gn = n0 + g * 64 + tx * 4;
+            const int gn = n0 + g * 64 + tx * T::GW;
             float* crow = C + (size_t)gm * ldc + gn;
-            const float2 p0 = acc[i][2 * g], p1 = acc[i][2 * g + 1];
-            if (gn + 4 <= N) {
-                *reinterpret_cast<float4*>(crow) = make_float4(p0.x, p0.y, p1.x, p1.y);
-            } else {
-                const float v4[4] = {p0.x, p0.y, p1.x, p1.y};
+            float v[T::GW];
 #pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    if (gn + j < N) crow[j] = v4[j];
+            for (int p = 0; p < T::GW / 2; ++p) {
+                v[2 * p] = acc[i][g * (T::GW / 2) + p].x;
+                v[2 * p + 1] = acc[i][g * (T::GW / 2) + p].y;
+            }
+            if (gn + T::GW <= N) {
+                stg_vec<T::GW>(crow, v);
+            } else {
+#pragma unroll
+                for (int j = 0; j < T::GW; ++j)
+                    if (gn + j < N) crow[j] = v[j];
             }
         }
     }
 }
 
-__global__ void __launch_bounds__(kV2Threads, 1) sgemm_v2_kernel(const float* __restrict__ A, const float* __restrict__ B,
-                                                                  float* __restrict__ C, int M, int N, int K, int lda,
-                                                                  int ldb, int ldc) {
+template <int TN>
+__global__ void __launch_bounds__(V2T<TN>::Threads, 1)
+    sgemm_v2_kernel(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C, int M, int N,
+                    int K, int lda, int ldb, int ldc) {
+    using T = V2T<TN>;
     extern __shared__ __align__(16) float v2_smem[];
     const int m0 = blockIdx.y * kV2BM, n0 = blockIdx.x * kV2BN;
-    float2 acc[8][4];  // acc[row][column pair]
+    float2 acc[8][T::NP];  // acc[row][column pair]
 #pragma unroll
     for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = make_float2(0.f, 0.f);
-    v2_mainloop(A, B, M, N, lda, ldb, m0, n0, 0, K, v2_smem, acc);
-    v2_store(C, M, N, ldc, m0, n0, acc);
+        for (int j = 0; j < T::NP; ++j) acc[i][j] = make_float2(0.f, 0.f);
+    v2_mainloop<TN>(A, B, M, N, lda, ldb, m0, n0, 0, K, v2_smem, acc);
+    v2_store<TN>(C, M, N, ldc, m0, n0, acc);
 }
 
 // ------------------------------------------------------------ stream-K
@@ -578,10 +620,13 @@ __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
     return v;
 }
 
-__global__ void __launch_bounds__(kV2Threads, 1)
+constexpr int kSkThreads = V2T<kV2TNStreamK>::Threads;
+__global__ void __launch_bounds__(kSkThreads, 1)
     sgemm_sk_kernel(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C, int M, int N,
                     int K, int lda, int ldb, int ldc, float4* __restrict__ ws, unsigned* __restrict__ flags,
                     unsigned epoch) {
+    constexpr int TN = kV2TNStreamK;
+    using T = V2T<TN>;
     extern __shared__ __align__(16) float v2_smem[];
     __shared__ int s_ok;
     const int tid = threadIdx.x;
@@ -598,19 +643,19 @@ __global__ void __launch_bounds__(kV2Threads, 1)
         const int kb = (int)(u - tile_u0);
         const int ke = (int)min((long long)iters, u_end - tile_u0);
         const int m0 = (t / nt) * kV2BM, n0 = (t % nt) * kV2BN;
-        float2 acc[8][4];
+        float2 acc[8][T::NP];
 #pragma unroll
         for (int i = 0; i < 8; ++i)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) acc[i][j] = make_float2(0.f, 0.f);
-        v2_mainloop(A, B, M, N, lda, ldb, m0, n0, kb * kV2BK, min(K, ke * kV2BK), v2_smem, acc);
+            for (int j = 0; j < T::NP; ++j) acc[i][j] = make_float2(0.f, 0.f);
+        v2_mainloop<TN>(A, B, M, N, lda, ldb, m0, n0, kb * kV2BK, min(K, ke * kV2BK), v2_smem, acc);
         if (kb != 0) {
             // Not the owner: park the partial tile, then raise the flag.
-            float4* dst = ws + (size_t)c * (16 * kV2Threads);
+            float4* dst = ws + (size_t)c * (T::Park * T::Threads);
 #pragma unroll
-            for (int v = 0; v < 16; ++v) {
-                const int i = v >> 1, j = (v & 1) * 2;
-                __stcg(dst + v * kV2Threads + tid,
+            for (int v = 0; v < T::Park; ++v) {
+                const int i = v / (T::NP / 2), j = (v % (T::NP / 2)) * 2;
+                __stcg(dst + v * T::Threads + tid,
                        make_float4(acc[i][j].x, acc[i][j].y, acc[i][j + 1].x, acc[i][j + 1].y));
             }
             __syncthreads();
@@ -644,11 +689,11 @@ __global__ void __launch_bounds__(kV2Threads, 1)
                     }
                     __syncthreads();
                     if (s_ok) {
-                        const float4* src = ws + (size_t)q * (16 * kV2Threads);
+                        const float4* src = ws + (size_t)q * (T::Park * T::Threads);
 #pragma unroll
-                        for (int v = 0; v < 16; ++v) {
-                            const int i = v >> 1, j = (v & 1) * 2;
-                            const float4 p4 = __ldcg(src + v * kV2Threads + tid);
+                        for (int v = 0; v < T::Park; ++v) {
+                            const int i = v / (T::NP / 2), j = (v % (T::NP / 2)) * 2;
+                            const float4 p4 = __ldcg(src + v * T::Threads + tid);
                             acc[i][j] = __fadd2_rn(acc[i][j], make_float2(p4.x, p4.y));
                             acc[i][j + 1] = __fadd2_rn(acc[i][j + 1], make_float2(p4.z, p4.w));
                         }
@@ -657,7 +702,7 @@ __global__ void __launch_bounds__(kV2Threads, 1)
                     if (qe >= tile_u1) break;
                 }
             }
-            v2_store(C, M, N, ldc, m0, n0, acc);
+            v2_store<TN>(C, M, N, ldc, m0, n0, acc);
         }
         u = tile_u0 + ke;
     }
@@ -665,17 +710,19 @@ __global__ void __launch_bounds__(kV2Threads, 1)
 
 static int launch_v2(const float* A, const float* B, float* C, int M, int N, int K, int lda, int ldb, int ldc,
                      cudaStream_t stream) {
+    constexpr int TN = kV2TNDense;
     const int smem = (int)(sizeof(float) * kV2Stages * (kV2AStage + kV2BStage));
     static thread_local uint64_t configured = 0;
     int dev = 0;
     cudaGetDevice(&dev);
     if (!(configured & (1ull << dev))) {
-        if (cudaFuncSetAttribute(sgemm_v2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+        if (cudaFuncSetAttribute(sgemm_v2_kernel<TN>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+            cudaSuccess)
             return GPLK_STATUS_LAUNCH_FAIL;
         configured |= 1ull << dev;
     }
     const int nt = (N + kV2BN - 1) / kV2BN, mt = (M + kV2BM - 1) / kV2BM;
-    sgemm_v2_kernel<<<dim3(nt, mt), kV2Threads, smem, stream>>>(A, B, C, M, N, K, lda, ldb, ldc);
+    sgemm_v2_kernel<TN><<<dim3(nt, mt), V2T<TN>::Threads, smem, stream>>>(A, B, C, M, N, K, lda, ldb, ldc);
     return launch_status(cudaGetLastError());
 }
 
@@ -708,7 +755,7 @@ static int launch_sk(const float* A, const float* B, float* C, int M, int N, int
         configured |= 1ull << dev;
     }
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sgemm_sk_kernel, kV2Threads, (size_t)smem) !=
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sgemm_sk_kernel, kSkThreads, (size_t)smem) !=
             cudaSuccess ||
         per_sm < 1)
         return GPLK_STATUS_UNSUPPORTED;
@@ -723,7 +770,7 @@ static int launch_sk(const float* A, const float* B, float* C, int M, int N, int
             if (s.device == dev && s.stream == stream && s.ctas == G) slot = &s;
         if (!slot) {
             SkSlot s{dev, stream, G, nullptr, nullptr, 0u};
-            if (cudaMalloc(&s.ws, (size_t)G * 16 * kV2Threads * sizeof(float4)) != cudaSuccess)
+            if (cudaMalloc(&s.ws, (size_t)G * V2T<kV2TNStreamK>::Park * kSkThreads * sizeof(float4)) != cudaSuccess)
                 return GPLK_STATUS_CUDA_ERROR;
             if (cudaMalloc(&s.flags, (size_t)G * sizeof(unsigned)) != cudaSuccess) {
                 cudaFree(s.ws);
@@ -743,7 +790,7 @@ static int launch_sk(const float* A, const float* B, float* C, int M, int N, int
         epoch = slot->epoch;
     }
     void* args[] = {&A, &B, &C, &M, &N, &K, &lda, &ldb, &ldc, &ws, &flags, &epoch};
-    if (cudaLaunchCooperativeKernel((const void*)sgemm_sk_kernel, dim3((unsigned)G), dim3(kV2Threads), args,
+    if (cudaLaunchCooperativeKernel((const void*)sgemm_sk_kernel, dim3((unsigned)G), dim3(kSkThreads), args,
                                     (size_t)smem, stream) != cudaSuccess)
         return GPLK_STATUS_LAUNCH_FAIL;
     return launch_status(cudaGetLastError());
