@@ -24,7 +24,7 @@
 // Flags carry a per-fabric epoch, so nothing is ever reset. Every wait is
 // bounded (2 s by default): on timeout the kernel records
 // GPLK_STATUS_DEVICE_TIMEOUT with the site and returns; no trap. The grid is
-// launched cooperatively (all blocks co-resident) with one block per SM.
+// launched cooperatively (all blocks co-resident) with two blocks per SM.
 // No multicast of any kind: plain peer loads and stores only.
 #include <cstring>
 
@@ -81,12 +81,10 @@ __device__ __forceinline__ void add_bf16x2(float& lo, float& hi, uint32_t v) {
     hi += __uint_as_float(v & 0xFFFF0000u);
 }
 
-// FP32 elements: four per vector, summed in rank order.
+// Sums of one 16-byte vector from every rank, in rank order 0..W-1 (so all
+// ranks produce identical bits). FP32: four elements per vector.
 template <int W>
-__device__ __forceinline__ uint4 reduce_vec_f32(const Args& a, size_t i) {
-    uint4 v[W];
-#pragma unroll
-    for (int q = 0; q < W; ++q) v[q] = a.src[q][i];
+__device__ __forceinline__ uint4 sum_f32(const uint4 (&v)[W]) {
     float s0 = __uint_as_float(v[0].x), s1 = __uint_as_float(v[0].y), s2 = __uint_as_float(v[0].z),
           s3 = __uint_as_float(v[0].w);
 #pragma unroll
@@ -99,11 +97,9 @@ __device__ __forceinline__ uint4 reduce_vec_f32(const Args& a, size_t i) {
     return make_uint4(__float_as_uint(s0), __float_as_uint(s1), __float_as_uint(s2), __float_as_uint(s3));
 }
 
+// BF16: eight elements per vector, summed in FP32 and rounded once.
 template <int W>
-__device__ __forceinline__ uint4 reduce_vec(const Args& a, size_t i) {
-    uint4 v[W];
-#pragma unroll
-    for (int q = 0; q < W; ++q) v[q] = a.src[q][i];  // all loads in flight before the sum
+__device__ __forceinline__ uint4 sum_bf16(const uint4 (&v)[W]) {
     float s[8];
     s[0] = __uint_as_float(v[0].x << 16);
     s[1] = __uint_as_float(v[0].x & 0xFFFF0000u);
@@ -124,8 +120,25 @@ __device__ __forceinline__ uint4 reduce_vec(const Args& a, size_t i) {
                       pack_bf16x2(s[6], s[7]));
 }
 
+// Reduces U vectors, `stride` apart from index i, and pushes each sum to
+// every rank. All U x W loads are in flight before the first sum.
+template <int W, bool F32, int U>
+__device__ __forceinline__ void reduce_push(const Args& a, size_t i, size_t stride) {
+    uint4 v[U][W];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int q = 0; q < W; ++q) v[u][q] = a.src[q][i + u * stride];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const uint4 r = F32 ? sum_f32<W>(v[u]) : sum_bf16<W>(v[u]);
+#pragma unroll
+        for (int q = 0; q < W; ++q) a.dst[q][i + u * stride] = r;
+    }
+}
+
 template <int W, bool F32>
-__global__ void __launch_bounds__(kThreads) allreduce_kernel(const Args a) {
+__global__ void __launch_bounds__(kThreads, 2) allreduce_kernel(const Args a) {
     unsigned* my_flags = a.flags[a.rank];
     // ---- entry: announce, then wait for every rank (one thread per block)
     if (blockIdx.x == 0 && threadIdx.x < (unsigned)W) st_release_sys(a.flags[threadIdx.x] + kEntry + a.rank, a.epoch);
@@ -141,11 +154,12 @@ __global__ void __launch_bounds__(kThreads) allreduce_kernel(const Args a) {
         const size_t lo = (size_t)a.rank * a.chunk16;
         const size_t hi = lo + a.chunk16 < a.n16 ? lo + a.chunk16 : a.n16;
         const size_t stride = (size_t)gridDim.x * blockDim.x;
-        for (size_t i = lo + (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < hi; i += stride) {
-            const uint4 r = F32 ? reduce_vec_f32<W>(a, i) : reduce_vec<W>(a, i);
-#pragma unroll
-            for (int q = 0; q < W; ++q) a.dst[q][i] = r;
-        }
+        // Two vectors per thread per step: 2 x W loads in flight. Measured
+        // at N = 2, 256 MiB: 623 -> 648 GB/s bus bandwidth (655 together
+        // with two blocks per SM).
+        size_t i = lo + (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+        for (; i + stride < hi; i += 2 * stride) reduce_push<W, F32, 2>(a, i, stride);
+        if (i < hi) reduce_push<W, F32, 1>(a, i, stride);
     }
     // ---- exit: the last block of this rank tells every rank, block 0 waits
     __threadfence_system();
@@ -207,7 +221,7 @@ extern "C" int gplk_fabric_create(int rank, int world, size_t bytes, gplk_fabric
         return GPLK_STATUS_CUDA_ERROR;
     }
     memcpy(handle, &h, sizeof(h));
-    f->blocks = d.sm_count;  // one block per SM; co-residency is checked by the cooperative launch
+    f->blocks = 2 * d.sm_count;  // two blocks per SM; co-residency is checked by the cooperative launch
     *out = f;
     return GPLK_STATUS_OK;
 }
@@ -257,7 +271,7 @@ extern "C" int gplk_fabric_create_local(int ndev, const int* devices, size_t byt
         f->world = ndev;
         f->bytes = bytes;
         f->device = devices[i];
-        f->blocks = d.sm_count;
+        f->blocks = 2 * d.sm_count;
         f->local = true;
         void* p = nullptr;
         if (cudaMalloc(&p, fabric::kFlagBytes + bytes) != cudaSuccess ||
