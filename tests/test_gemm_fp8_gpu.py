@@ -41,7 +41,8 @@ def _run(gplk, qa, sa, qb, sb, cuda):
 
 
 @pytest.mark.parametrize("mnk", [(128, 256, 128), (256, 256, 256), (512, 512, 1024), (1024, 768, 512), (300, 520, 256), (136, 264, 384),
-                                 (200, 300, 512), (129, 257, 144), (1, 1, 16), (640, 1280, 2048)])
+                                 (200, 300, 512), (129, 257, 144), (1, 1, 16), (640, 1280, 2048),
+                                 (4352, 264, 128)])  # 17 pair-tile rows: a second, one-row raster group
 def test_fp8_full_vs_oracle(mnk, gplk, oracle, cuda):
     M, N, K = mnk
     qa, sa, qb, sb = _operands(oracle, M, N, K, seed=M * 7 + N)

@@ -57,8 +57,11 @@ def _rel(x: np.ndarray, ref: np.ndarray) -> float:
     return float(np.linalg.norm(x.astype(np.float64) - ref) / max(np.linalg.norm(ref), 1e-30))
 
 
+# (4608, 384, 128) and (4352, 272, 64) give more than one raster group of
+# 256-row pair tiles (8 per group for 2- and 4-byte operands, 16 for INT8),
+# so odd groups walk N backwards, the last group ragged.
 SHAPES = [(256, 256, 256), (1024, 1024, 1024), (512, 384, 1024), (264, 520, 128), (128, 256, 512),
-          (768, 1, 64), (2048, 512, 4096)]
+          (768, 1, 64), (2048, 512, 4096), (4608, 384, 128), (4352, 272, 64)]
 
 
 @pytest.mark.parametrize("prec", ["bf16", "f16", "tf32", "i8"])
