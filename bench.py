@@ -77,6 +77,9 @@ def parse_args():
     ap.add_argument("--fabric", choices=["nccl", "gplk"], default="nccl",
                     help="powervirus fabric step: NCCL all_reduce, or gplk_fabric_allreduce_bf16 over NVLink peers")
     ap.add_argument("--fabric-mib", type=int, default=256, help="fabric allreduce size (BF16), MiB")
+    ap.add_argument("--sgemm-n", type=int, default=1024,
+                    help="sgemm workload size M = N = K (1024 is the parity configuration; the rung's --size "
+                         "default is 4096)")
     ap.add_argument("--mix", default="4,1,2", help="powervirus role weights tensor,fma,dram[,sfu,int32,smem,l2,atomic]")
     ap.add_argument("--budget-us", type=float, default=1000.0, help="powervirus launch time box")
     ap.add_argument("--duty-on-ms", type=float, default=100.0)
@@ -440,7 +443,7 @@ def bench_gemm(args, dist: Dist) -> dict:
     stream = torch.cuda.current_stream(dev)
     w = args.workload
     if w == "sgemm":
-        n = 1024
+        n = args.sgemm_n
         A = torch.rand(n, n, device=dev, generator=g) * 2 - 1
         B = torch.rand(n, n, device=dev, generator=g) * 2 - 1
         C = torch.empty(n, n, device=dev)
@@ -450,7 +453,7 @@ def bench_gemm(args, dist: Dist) -> dict:
             flush.zero_()  # 256 MiB write: evicts the 12 MiB working set from L2
             gplk.sgemm(A, B, C, stream=stream)
 
-        dtype, workload = "f32", "FP32 SGEMM C = A*B row-major, M=N=K=1024, U[-1,1)"
+        dtype, workload = "f32", f"FP32 SGEMM C = A*B row-major, M=N=K={n}, U[-1,1)"
         launches_per_step = 2
     elif w in NN_GEMMS:
         n = 8192
@@ -537,7 +540,8 @@ def bench_gemm(args, dist: Dist) -> dict:
                    "parallelism": f"replicas x{dist.world}"},
         "roofline": {"bound": "tensor" if w != "sgemm" else "fp32-simt", "achieved": round(achieved, 1),
                      "peak": round(peak, 1), "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
-                     "traffic": NCU_TRAFFIC.get(w), "peak_source": "nominal dense"},
+                     "traffic": NCU_TRAFFIC.get(w) if (w != "sgemm" or n == 1024) else None,
+                     "peak_source": "nominal dense"},
         "clocks": sampler.summary(),
         "gpu_launches": args.steps * (1 if w != "sgemm" else 1),
     }

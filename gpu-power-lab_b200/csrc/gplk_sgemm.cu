@@ -405,8 +405,8 @@ static int launch_split2(const float* A, const float* B, float* C, int M, int N,
 }
 
 // ------------------------------------------------------------ cp.async + FFMA2 main loop
-// 128 x 128 tiles, 256 threads, 8 x 8 outputs per thread (rows ty*4+i and
-// 64+ty*4+i, columns tx*4+j and 64+tx*4+j), BK = 16, a 3-stage ring filled
+// 128 x 128 tiles, 8 x 16 outputs per thread (128 threads) or 8 x 8 (256
+// threads; layout in V2T below), BK = 16, a 3-stage ring filled
 // by cp.async straight from global memory (no register staging). A stays
 // K-major in shared memory (one 128-bit load = four k of one row), B stays
 // N-major. The FFMAs issue as Blackwell's paired FP32 FMA (__ffma2_rn: two
@@ -414,13 +414,18 @@ static int launch_split2(const float* A, const float* B, float* C, int M, int N,
 // halving the FMA issue slots. Each output is one FMA chain over k in order
 // (or, under stream-K below, a fixed-order sum of a few such chains).
 constexpr int kV2BM = 128, kV2BN = 128, kV2BK = 16, kV2Stages = 3;
-// Thread layout for TN outputs per thread along N (each thread: 8 rows x TN
-// columns, in two 64-column halves).
+// Thread layout for TN outputs per thread along N. Thread (tx, ty) owns rows
+// ty + 16 i (i < 8) and TN / 4 groups of four columns, group h at
+// h * GS + 4 tx. Both are conflict-free in shared memory: a warp's A reads
+// hit rows of consecutive ty (80-byte pitch: distinct 16-byte bank groups)
+// and its B reads cover 4 TX contiguous floats.
 template <int TN>
 struct V2T {
-    static constexpr int GW = TN / 2;           // columns per thread in each 64-column half
+    static_assert(TN == 8 || TN == 16, "8 x 8 or 8 x 16 per thread");
     static constexpr int NP = TN / 2;           // column pairs per thread
+    static constexpr int NG = TN / 4;           // column groups of four per thread
     static constexpr int TX = kV2BN / TN;       // threads along N
+    static constexpr int GS = 4 * TX;           // column stride between a thread's groups
     static constexpr int Threads = TX * 16;     // 16 threads along M
     static constexpr int Park = 2 * TN;         // float4 per thread in a parked partial tile
 };
@@ -453,25 +458,16 @@ __device__ __forceinline__ void v2_ktile(const float* as, const float* bs, int t
         float4 af[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const int row = (i >> 2) * 64 + ty * 4 + (i & 3);
-            af[i] = *reinterpret_cast<const float4*>(as + row * kV2APitch + kq);
+            af[i] = *reinterpret_cast<const float4*>(as + (ty + 16 * i) * kV2APitch + kq);
         }
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
             float2 bp[T::NP];
 #pragma unroll
-            for (int g = 0; g < 2; ++g) {
-                const float* src = bs + (kq + kk) * kV2BN + g * 64 + tx * T::GW;
-                if constexpr (T::GW % 4 == 0) {
-#pragma unroll
-                    for (int h = 0; h < T::GW / 4; ++h) {
-                        const float4 b = *reinterpret_cast<const float4*>(src + 4 * h);
-                        bp[g * (T::GW / 2) + 2 * h] = make_float2(b.x, b.y);
-                        bp[g * (T::GW / 2) + 2 * h + 1] = make_float2(b.z, b.w);
-                    }
-                } else {
-                    bp[g] = *reinterpret_cast<const float2*>(src);
-                }
+            for (int h = 0; h < T::NG; ++h) {
+                const float4 b = *reinterpret_cast<const float4*>(bs + (kq + kk) * kV2BN + h * T::GS + tx * 4);
+                bp[2 * h] = make_float2(b.x, b.y);
+                bp[2 * h + 1] = make_float2(b.z, b.w);
             }
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
@@ -546,8 +542,8 @@ __device__ __forceinline__ void v2_mainloop(const float* __restrict__ A, const f
     __syncthreads();
 }
 
-// Stores the tile's accumulators (rows ty*4+i and 64+ty*4+i, columns
-// tx*T::GW.. and 64+tx*T::GW..) with bounds checks.
+// Stores the tile's accumulators (rows ty + 16 i, column groups h * GS +
+// 4 tx) with bounds checks.
 template <int TN>
 __device__ __forceinline__ void v2_store(float* __restrict__ C, int M, int N, int ldc, int m0, int n0,
                                          const float2 (&acc)[8][TN / 2]) {
@@ -556,23 +552,18 @@ __device__ __forceinline__ void v2_store(float* __restrict__ C, int M, int N, in
     const int tx = tid % T::TX, ty = tid / T::TX;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        const int gm = m0 + (i >> 2) * 64 + ty * 4 + (i & 3);
+        const int gm = m0 + ty + 16 * i;
         if (gm >= M) continue;
 #pragma unroll
-        for (int g = 0; g < 2; ++g) {
-            const int gn = n0 + g * 64 + tx * T::GW;
+        for (int h = 0; h < T::NG; ++h) {
+            const int gn = n0 + h * T::GS + tx * 4;
             float* crow = C + (size_t)gm * ldc + gn;
-            float v[T::GW];
-#pragma unroll
-            for (int p = 0; p < T::GW / 2; ++p) {
-                v[2 * p] = acc[i][g * (T::GW / 2) + p].x;
-                v[2 * p + 1] = acc[i][g * (T::GW / 2) + p].y;
-            }
-            if (gn + T::GW <= N) {
-                stg_vec<T::GW>(crow, v);
+            const float v[4] = {acc[i][2 * h].x, acc[i][2 * h].y, acc[i][2 * h + 1].x, acc[i][2 * h + 1].y};
+            if (gn + 4 <= N) {
+                stg_vec<4>(crow, v);
             } else {
 #pragma unroll
-                for (int j = 0; j < T::GW; ++j)
+                for (int j = 0; j < 4; ++j)
                     if (gn + j < N) crow[j] = v[j];
             }
         }
