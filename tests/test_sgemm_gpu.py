@@ -33,9 +33,13 @@ def test_sgemm_1024_seed0(gplk, oracle, cuda):
     assert float(np.max(np.abs(got - want))) <= TOL * float(np.max(np.abs(want)))
 
 
+# (2048, 2304, 300) and (2000, 2300, 200) fill two whole waves of 128 x 128
+# tiles (one tile per block, 8 x 16 per thread, ragged edges in the second);
+# (1000, 1000, 333), (768, 1024, 1024) and (1024, 2048, 4096) run stream-K.
 @pytest.mark.parametrize("mnk", [(1, 1, 1), (33, 17, 5), (100, 130, 257), (257, 129, 1000),
                                  (64, 64, 16), (128, 256, 64), (2048, 512, 300), (3000, 2000, 128),
-                                 (1000, 1000, 333), (768, 1024, 1024), (1024, 2048, 4096)])
+                                 (1000, 1000, 333), (768, 1024, 1024), (1024, 2048, 4096),
+                                 (2048, 2304, 300), (2000, 2300, 200)])
 def test_sgemm_shapes(mnk, gplk, oracle, cuda):
     M, N, K = mnk
     A = oracle.uniform_f32(M * K, seed=M, lo=-1.0, hi=1.0).reshape(M, K)
