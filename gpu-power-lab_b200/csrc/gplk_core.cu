@@ -6,6 +6,7 @@
 
 #include <cstdio>
 #include <mutex>
+#include <utility>
 
 #include "gplk_ptx.cuh"
 
@@ -54,6 +55,24 @@ static int require_sm100(DeviceInfo* info) {
 static int launch_status(cudaError_t e) {
     if (e == cudaSuccess) return GPLK_STATUS_OK;
     return GPLK_STATUS_LAUNCH_FAIL;
+}
+
+// Launches `kernel` with programmatic stream serialisation, so it may begin
+// (up to its pdl_wait()) while the previous kernel on `stream` finishes.
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // cuTensorMapEncodeTiled reached through the runtime's driver entry point,

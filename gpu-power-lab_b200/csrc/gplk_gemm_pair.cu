@@ -228,6 +228,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     cluster_sync();
     tc_fence_after();
     const uint32_t tmem = sm.tmem_base;
+    // Launched with programmatic stream serialisation: the set-up above may
+    // overlap the previous kernel's tail; nothing below touches global
+    // memory before that kernel has completed. The next GEMM on the stream
+    // may then be launched into SMs as they free up.
+    pdl_wait();
+    pdl_launch_dependents();
 
     if (warp == 0) {
         // TMA producer (one thread per CTA); both CTAs' bytes complete on the
@@ -519,8 +525,8 @@ static int launch(const void* A, const void* B, void* D, int M, int N, int K, cu
     }
     const int tiles = p.m_tiles * p.n_tiles;
     const int clusters = capacity[dev] < tiles ? capacity[dev] : tiles;
-    gemm_pair_kernel<C><<<2 * clusters, kThreads, kSmemBytes, stream>>>(tmA, tmB, tmD, p);
-    return launch_status(cudaGetLastError());
+    return launch_status(launch_pdl(gemm_pair_kernel<C>, dim3(2 * clusters), dim3(kThreads), kSmemBytes, stream,
+                                    tmA, tmB, tmD, p));
 }
 
 // Arguments shared by the four entry points. Operand pitches must be

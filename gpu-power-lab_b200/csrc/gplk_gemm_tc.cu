@@ -132,6 +132,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = sm.tmem_base;
+    // Launched with programmatic stream serialisation: the set-up above may
+    // overlap the previous kernel's tail; nothing below touches global
+    // memory before that kernel has completed. The next GEMM on the stream
+    // may then be launched into SMs as they free up.
+    pdl_wait();
+    pdl_launch_dependents();
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
@@ -417,8 +423,8 @@ static int launch(const uint8_t* A, const uint8_t* B, const uint8_t* SFA, const 
     }
     const int tiles = p.m_tiles * p.n_tiles;
     const int grid = tiles < d.sm_count ? tiles : d.sm_count;
-    gemm_tc_kernel<NVF4><<<grid, kThreads, smem, stream>>>(tmA, tmB, tmD, p);
-    return launch_status(cudaGetLastError());
+    return launch_status(launch_pdl(gemm_tc_kernel<NVF4>, dim3(grid), dim3(kThreads), (size_t)smem, stream, tmA,
+                                    tmB, tmD, p));
 }
 
 }  // namespace gemm_tc

@@ -186,6 +186,16 @@ __device__ __forceinline__ void tc_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
+// Programmatic dependent launch. A kernel launched with programmatic stream
+// serialisation may start while the previous kernel on its stream is still
+// running; pdl_wait() blocks until that kernel has completed and its memory
+// is visible, so it must come before the first access to global memory the
+// previous kernel could have written. pdl_launch_dependents() lets the next
+// such kernel on the stream be launched (it still waits in pdl_wait()).
+// Both are no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Arrive once on `bar` when every tcgen05 op previously issued by this
 // thread has completed.
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
