@@ -4,9 +4,12 @@
  *
  * Every entry point:
  *   - takes plain device pointers, sizes and a CUDA stream;
- *   - allocates nothing and is stream-ordered (asynchronous: a device fault
- *     or a device-side wait timeout shows up at the caller's next sync and
- *     in gplk_status_read);
+ *   - is stream-ordered (asynchronous: a device fault or a device-side
+ *     wait timeout shows up at the caller's next sync and in
+ *     gplk_status_read) and allocates nothing per call; the exceptions are
+ *     named where they occur: gplk_fabric_create* allocate the fabric's
+ *     buffers, and gplk_sgemm_f32 allocates a stream's stream-K workspace
+ *     once, on that stream's first call that needs it;
  *   - returns a gplk_status code synchronously from argument and launch
  *     checks.
  *
