@@ -16,6 +16,8 @@ prints one JSON object (not collected by pytest; run on a GPU):
              runner/src/workload_gemm.c (oracle/ref_gemm_shim.c) vs
              gplk_gemm_{bf16,f16,tf32,i8}_nn, 8192^3, identical operands:
              random values and the rung's own 0x3c byte fill
+  ladder     FP8 (the reference's gemm_lt.cu) and BF16 (its cublasGemmEx
+             call) against libgplk at 1024 / 2048 / 4096, random operands
   nn_ref_calls  four reference cublasGemmEx calls each for BF16 and TF32 at
              8192^3 on random operands and nothing else timed: the launch
              list to put under ncu for the library kernels' DRAM traffic
@@ -201,6 +203,50 @@ def fp8(out):
     out["fp8_8192_TFLOPs"] = res
     L.gpl_lt_free(g)
     L.ref_lt_delete(g)
+
+
+def ladder(out):
+    """Smaller rungs of the FP8 and BF16 ladders (--size 1024 / 2048 / 4096),
+    random operands, back-to-back launches: the reference's gemm_lt.cu FP8
+    path and its cublasGemmEx BF16 call against libgplk."""
+    L = oracle.ref_lib()
+    cudart = ctypes.CDLL("libcudart.so.12")
+    cudart.cudaMemcpy.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int]
+    st = lambda: ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    res = {}
+    for n in (1024, 2048, 4096):
+        tf = lambda ms: round(2 * n ** 3 / (ms / 1e3) / 1e12, 1)
+        g = L.ref_lt_new()
+        assert L.gpl_lt_init(g, oracle.PREC["fp8"], n, torch.cuda.current_stream().cuda_stream) == 0
+        ptrs = (ctypes.c_void_p * 7)()
+        L.ref_lt_ptrs(g, ptrs)
+        A = torch.randint(0, 0x7E, (n, n), dtype=torch.uint8, device="cuda")
+        B = torch.randint(0, 0x7E, (n, n), dtype=torch.uint8, device="cuda")
+        D = torch.empty(n, n, dtype=torch.bfloat16, device="cuda")
+        s1 = torch.ones(1, device="cuda")
+        torch.cuda.synchronize()
+        assert cudart.cudaMemcpy(ptrs[0], A.data_ptr(), n * n, 3) == 0
+        assert cudart.cudaMemcpy(ptrs[1], B.data_ptr(), n * n, 3) == 0
+        torch.cuda.synchronize()
+        case = {}
+        for name, fn in (("fp8_reference_gemm_lt_cublaslt", lambda: L.gpl_lt_enqueue(g, 1)),
+                         ("fp8_gplk_gemm_fp8_tn", lambda: gplk.gemm_fp8_tn(A, B, D, s1, s1))):
+            ms, mhz, w = sustained(fn)
+            case[name] = {"tflops": tf(ms), "sm_mhz": mhz, "watts": w}
+        L.gpl_lt_free(g)
+        L.ref_lt_delete(g)
+        Ab = (torch.rand(n, n, device="cuda") * 2 - 1).to(torch.bfloat16)
+        Bb = (torch.rand(n, n, device="cuda") * 2 - 1).to(torch.bfloat16)
+        Db = torch.empty(n, n, dtype=torch.bfloat16, device="cuda")
+        for name, fn in (("bf16_reference_cublasGemmEx",
+                          lambda: L.ref_gemm_ex(4, Ab.data_ptr(), Bb.data_ptr(), Db.data_ptr(), n, st())),
+                         ("bf16_gplk_gemm_bf16_nn", lambda: gplk.gemm_nn("bf16", Ab, Bb, Db, n, n, n))):
+            ms, mhz, w = sustained(fn)
+            case[name] = {"tflops": tf(ms), "sm_mhz": mhz, "watts": w}
+        res[n] = case
+        del A, B, D, Ab, Bb, Db
+        torch.cuda.empty_cache()
+    out["ladder_TFLOPs"] = res
 
 
 def nvfp4(out):
