@@ -9,6 +9,7 @@
 // Each output is one FP32 FFMA chain over k = 0..K-1 in order, so the result
 // differs from a double-accumulated host loop only by FP32 rounding.
 #include <mutex>
+#include <thread>
 #include <vector>
 
 #include "gplk_ptx.cuh"
@@ -718,13 +719,15 @@ static int launch_v2(const float* A, const float* B, float* C, int M, int N, int
 }
 
 // One stream-K workspace per (device, stream): partial-tile slots and flags
-// for one CTA per SM. Concurrent GEMMs on different streams never share one;
-// GEMMs on one stream are ordered by the stream. Allocated on first use
+// for one CTA per SM. Concurrent GEMMs on different streams never share one
+// (cudaStreamPerThread is a different stream in each host thread, so it is
+// keyed by thread too); GEMMs on one stream are ordered by the stream. Allocated on first use
 // (cudaMalloc, so the first call for a stream must not be inside a CUDA
 // graph capture) and kept for the life of the process.
 struct SkSlot {
     int device;
     cudaStream_t stream;
+    std::thread::id thread;  // set only for cudaStreamPerThread, whose handle names one stream per thread
     int ctas;
     float4* ws;
     unsigned* flags;
@@ -756,11 +759,13 @@ static int launch_sk(const float* A, const float* B, float* C, int M, int N, int
     unsigned epoch = 0;
     {
         std::lock_guard<std::mutex> lock(g_sk_mu);
+        const std::thread::id thread =
+            stream == cudaStreamPerThread ? std::this_thread::get_id() : std::thread::id();
         SkSlot* slot = nullptr;
         for (SkSlot& s : g_sk_slots)
-            if (s.device == dev && s.stream == stream && s.ctas == G) slot = &s;
+            if (s.device == dev && s.stream == stream && s.thread == thread && s.ctas == G) slot = &s;
         if (!slot) {
-            SkSlot s{dev, stream, G, nullptr, nullptr, 0u};
+            SkSlot s{dev, stream, thread, G, nullptr, nullptr, 0u};
             if (cudaMalloc(&s.ws, (size_t)G * V2T<kV2TNStreamK>::Park * kSkThreads * sizeof(float4)) != cudaSuccess)
                 return GPLK_STATUS_CUDA_ERROR;
             if (cudaMalloc(&s.flags, (size_t)G * sizeof(unsigned)) != cudaSuccess) {
