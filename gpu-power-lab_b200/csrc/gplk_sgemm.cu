@@ -1,13 +1,21 @@
 // gplk_sgemm.cu - true-FP32 SIMT SGEMM (FFMA, no TF32), row-major.
 //
-// Register-blocked tiles: a CTA computes BM x BN of C, each thread TM x TN
-// split into two halves along each dimension (rows ty*TM/2 and BM/2 +
-// ty*TM/2, likewise for columns) so shared-memory reads of a warp are either
-// broadcasts or contiguous 128-bit loads. K is walked in BK slices through
-// a double-buffered shared-memory ring; the next slice is fetched into
-// registers while the current one is multiplied.
-// Each output is one FP32 FFMA chain over k = 0..K-1 in order, so the result
-// differs from a double-accumulated host loop only by FP32 rounding.
+// Three kernel families, chosen by gplk_sgemm_f32 at the end of the file:
+//   * 16-byte-aligned operands (the runner's case): the cp.async + paired
+//     FFMA main loop (sgemm_v2_kernel, 128 x 128 tiles, 8 x 16 outputs per
+//     thread), or, when the tiles leave the last wave of SMs ragged,
+//     stream-K over one block per SM (sgemm_sk_kernel, 8 x 8 per thread);
+//   * anything else: the register-staged kernels below (sgemm_kernel, and a
+//     2-CTA cluster split of K for problems with few tiles).
+// The register-staged kernels: a CTA computes BM x BN of C, each thread
+// TM x TN split into two halves along each dimension (rows ty*TM/2 and
+// BM/2 + ty*TM/2, likewise for columns) so shared-memory reads of a warp are
+// either broadcasts or contiguous 128-bit loads. K is walked in BK slices
+// through a double-buffered shared-memory ring; the next slice is fetched
+// into registers while the current one is multiplied.
+// Each output is one FP32 FFMA chain over k in order (split-K and stream-K
+// add a few such chains in a fixed order), so the result differs from a
+// double-accumulated host loop only by FP32 rounding.
 #include <mutex>
 #include <thread>
 #include <vector>
