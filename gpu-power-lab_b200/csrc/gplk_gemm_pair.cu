@@ -18,7 +18,9 @@
 // D is always M x N column-major.
 //
 // A persistent grid of 2-CTA clusters walks 256 x 256 output tiles in a
-// grouped order. Per cluster, one tcgen05.mma.cta_group::2 (M = 256,
+// grouped order (raster groups along M; odd groups walk N backwards). It is
+// launched with programmatic stream serialisation, so its set-up overlaps
+// the previous GEMM on the stream. Per cluster, one tcgen05.mma.cta_group::2 (M = 256,
 // N = 256) per 32 bytes of K; each CTA TMA-loads its own 128 rows of the A
 // tile and its own 128 rows (N) of the B tile with the 128-byte swizzle, no
 // cluster multicast. A pipeline stage holds two 128-byte slabs of K (64 KiB

@@ -5,7 +5,8 @@
 // convention (A and B K-major, D column-major M x N).
 //
 // One persistent CTA per SM walks output tiles of 128 x 256 in a grouped
-// (L2-friendly) order. Warp roles:
+// (L2-friendly) order, launched with programmatic stream serialisation (its
+// set-up overlaps the previous GEMM on the stream). Warp roles:
 //   warp 0      TMA producer: 2-D tiled loads of A (128 rows) and B (256
 //               rows), 128 bytes of K per stage with 128-byte swizzle, into a
 //               STAGES-deep shared-memory ring; NVFP4 adds 1-D bulk copies of
