@@ -529,7 +529,13 @@ def bench_gemm(args, dist: Dist) -> dict:
         kernel_s = ms / 1e3 / args.steps
     achieved = flops / kernel_s / 1e12
     value = dist.world * flops * args.steps / (ms_max / 1e3) / 1e12
-    peak = NOMINAL_TFLOPS[w]
+    peak, peak_source = NOMINAL_TFLOPS[w], "nominal dense"
+    scalar_ffma = None
+    if w == "sgemm":
+        # Scalar FFMA alone stays well below the nominal FP32 rate on B200
+        # (paired FFMA2 is what reaches it), so it is context, not the peak.
+        peak_source = "nominal: 148 SMs x 128 FP32 lanes x 2 flop x 1965 MHz"
+        scalar_ffma = round(fma_peak_tflops(dev, stream), 1)
     return {
         "metric": f"{w} TFLOP/s", "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": dist.world,
         "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms_max / args.steps, 4),
@@ -541,10 +547,39 @@ def bench_gemm(args, dist: Dist) -> dict:
         "roofline": {"bound": "tensor" if w != "sgemm" else "fp32-simt", "achieved": round(achieved, 1),
                      "peak": round(peak, 1), "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                      "traffic": NCU_TRAFFIC.get(w) if (w != "sgemm" or n == 1024) else None,
-                     "peak_source": "nominal dense"},
+                     "peak_source": peak_source,
+                     **({"scalar_ffma_measured_tflops": scalar_ffma} if scalar_ffma is not None else {})},
         "clocks": sampler.summary(),
         "gpu_launches": args.steps * (1 if w != "sgemm" else 1),
     }
+
+
+def fma_peak_tflops(dev, stream, inner: int = 10000) -> float:
+    """Scalar-FFMA throughput of this GPU, measured: gplk_powervirus_launch
+    with every warp slot on the FMA role and fixed work (each thread runs
+    eight dependent FFMA chains for inner x 16 steps), one 32-warp block per
+    SM, timed with CUDA events over three launches after two warm-up
+    launches."""
+    import gplk
+    import torch
+
+    role_map, _ = gplk.pv_role_map([0, 1, 0, 0, 0, 0, 0, 0])
+    role = torch.tensor(role_map, dtype=torch.uint8, device=dev)
+    buf = torch.zeros((64 << 10) // 4, device=dev)
+    sink = torch.zeros(1 + 1024, device=dev)
+    cfg = gplk.PvCfg(role_map=role.data_ptr(), stream_buf=buf.data_ptr(), stream_bytes=64 << 10,
+                     sink=sink.data_ptr(), blocks=0, inner=inner, budget_ns=0)
+    for _ in range(2):
+        gplk.powervirus_launch(cfg, stream=stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(3):
+        gplk.powervirus_launch(cfg, stream=stream)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    flops = 3 * sms * gplk.pv_block_threads() * 8 * inner * 16 * 2
+    return flops / (e0.elapsed_time(e1) / 1e3) / 1e12
 
 
 # ------------------------------------------------------------ powervirus rung
