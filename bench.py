@@ -535,7 +535,7 @@ def bench_gemm(args, dist: Dist) -> dict:
         # Scalar FFMA alone stays well below the nominal FP32 rate on B200
         # (paired FFMA2 is what reaches it), so it is context, not the peak.
         peak_source = "nominal: 148 SMs x 128 FP32 lanes x 2 flop x 1965 MHz"
-        scalar_ffma = round(fma_peak_tflops(dev, stream), 1)
+        scalar_ffma = fma_peak_tflops(dev, stream)
     return {
         "metric": f"{w} TFLOP/s", "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": dist.world,
         "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms_max / args.steps, 4),
@@ -548,18 +548,18 @@ def bench_gemm(args, dist: Dist) -> dict:
                      "peak": round(peak, 1), "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                      "traffic": NCU_TRAFFIC.get(w) if (w != "sgemm" or n == 1024) else None,
                      "peak_source": peak_source,
-                     **({"scalar_ffma_measured_tflops": scalar_ffma} if scalar_ffma is not None else {})},
+                     **({"scalar_ffma_measured": scalar_ffma} if scalar_ffma is not None else {})},
         "clocks": sampler.summary(),
         "gpu_launches": args.steps * (1 if w != "sgemm" else 1),
     }
 
 
-def fma_peak_tflops(dev, stream, inner: int = 10000) -> float:
+def fma_peak_tflops(dev, stream, inner: int = 10000, launches: int = 60) -> dict:
     """Scalar-FFMA throughput of this GPU, measured: gplk_powervirus_launch
     with every warp slot on the FMA role and fixed work (each thread runs
     eight dependent FFMA chains for inner x 16 steps), one 32-warp block per
-    SM, timed with CUDA events over three launches after two warm-up
-    launches."""
+    SM, `launches` launches (about a third of a second) timed with CUDA
+    events after two warm-up launches, with the SM clock sampled meanwhile."""
     import gplk
     import torch
 
@@ -571,15 +571,24 @@ def fma_peak_tflops(dev, stream, inner: int = 10000) -> float:
                      sink=sink.data_ptr(), blocks=0, inner=inner, budget_ns=0)
     for _ in range(2):
         gplk.powervirus_launch(cfg, stream=stream)
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(dev.index if dev.index is not None else 0, period_s=0.01)
+    sampler.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(3):
+    for _ in range(launches):
         gplk.powervirus_launch(cfg, stream=stream)
     e1.record(stream)
     torch.cuda.synchronize(dev)
+    sampler.stop()
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    flops = 3 * sms * gplk.pv_block_threads() * 8 * inner * 16 * 2
-    return flops / (e0.elapsed_time(e1) / 1e3) / 1e12
+    flops = launches * sms * gplk.pv_block_threads() * 8 * inner * 16 * 2
+    tflops = flops / (e0.elapsed_time(e1) / 1e3) / 1e12
+    clk = sampler.summary()
+    out = {"tflops": round(tflops, 1), "sm_mhz": clk.get("sm_mhz"), "power_w_median": clk.get("power_w_median")}
+    if clk.get("sm_mhz"):
+        out["frac_of_nominal_at_that_clock"] = round(tflops / (sms * 128 * 2 * clk["sm_mhz"] * 1e6 / 1e12), 4)
+    return out
 
 
 # ------------------------------------------------------------ powervirus rung
