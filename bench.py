@@ -280,6 +280,38 @@ def cpu_triad_gbps(seconds: float, n: int = 1 << 28, threads: int = 0) -> dict:
             "sample": f"{reps} host triads over 3 x 2^{n.bit_length() - 1} FP32 ({el:.1f} s)"}
 
 
+def cpu_sgemm_tflops(n: int, seconds: float) -> dict:
+    """The host C11 triple loop (the oracle's gplo_sgemm_f32_naive: row-major,
+    FP32 accumulate in k order) on the n^3 problem's operands, all cores with
+    OpenMP, and single-threaded on a row slab sized to about a tenth of
+    `seconds`. Reported beside the GPU number, not a target."""
+    sys.path.insert(0, str(REPO / "oracle"))
+    import oracle
+
+    A = oracle.uniform_f32(n * n, seed=0, lo=-1.0, hi=1.0).reshape(n, n)
+    B = oracle.uniform_f32(n * n, seed=1, lo=-1.0, hi=1.0).reshape(n, n)
+    nthreads = oracle.max_threads()
+    # Whole problem up to 1024^3; above that a row slab of about 2 GFLOP.
+    slab = n if n <= 1024 else max(16, (1 << 30) // (n * n))
+    As = A if slab == n else A[:slab].copy()
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        oracle.sgemm_f32_naive(As, B, nthreads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    rows = 16
+    t1 = time.perf_counter()
+    oracle.sgemm_f32_naive(A[:rows].copy(), B, 1)
+    one = 2.0 * rows * n * n / (time.perf_counter() - t1) / 1e12
+    what = f"{n}^3" if slab == n else f"a {slab}-row slab of the {n}^3 problem"
+    return {"value": round(2.0 * slab * n * n * reps / el / 1e12, 4), "unit": "TFLOP/s", "cores": nthreads,
+            "kind": "port", "single_thread_tflops": round(one, 5),
+            "sample": f"{reps} host triple-loop SGEMMs on {what}, {nthreads} threads ({el:.1f} s); "
+                      f"single thread timed on a {rows}-row slab"}
+
+
 # ------------------------------------------------------------ memstream
 
 def bench_memstream(args, dist: Dist) -> dict:
@@ -883,6 +915,8 @@ def main():
             line = bench_powervirus(args, dist)
         if dist.rank == 0 and dist.world == 1 and not args.no_cpu and args.workload == "memstream":
             line["cpu_baseline"] = cpu_triad_gbps(args.cpu_seconds)
+        if dist.rank == 0 and dist.world == 1 and not args.no_cpu and args.workload == "sgemm":
+            line["cpu_baseline"] = cpu_sgemm_tflops(args.sgemm_n, min(args.cpu_seconds, 10.0))
         if dist.rank == 0:
             print(json.dumps(line), flush=True)
     finally:
