@@ -860,6 +860,21 @@ def bench_fabric(args, dist: Dist) -> dict:
 def bench_reference(args, dist: Dist) -> dict | None:
     if dist.rank != 0:
         return None
+    if args.workload == "sgemm":
+        # The reference's SGEMM runs on the GPU (cublasGemmEx); its CPU
+        # counterpart is the host triple loop the parity oracle restates.
+        cpu = cpu_sgemm_tflops(args.sgemm_n, min(args.cpu_seconds, 10.0))
+        return {
+            "impl": "reference", "metric": "sgemm TFLOP/s", "value": cpu["value"], "unit": "TFLOP/s",
+            "n_gpus": dist.world, "steps": 1, "warmup": 0, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic, seeded",
+            "config": {"workload": f"FP32 SGEMM C = A*B row-major, M=N=K={args.sgemm_n}, U[-1,1)"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": cpu["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
+    if args.workload != "memstream":
+        return {"impl": "reference", "unavailable": f"no host implementation of the {args.workload} rung in the "
+                                                    "reference (its GEMMs run in cuBLAS / cuBLASLt on the GPU)"}
     sys.path.insert(0, str(REPO / "oracle"))
     import numpy as np
     import oracle
