@@ -5,7 +5,8 @@
  * Arrays as in the reference (runner/src/workload_memstream.cu:60-84):
  * size x size FP32 elements each, A and B shared (memset 0x3c), one C per
  * stream (zeroed). Each iteration is one gplk_triad_f32 launch per stream,
- * C = A + scalar * B, on the 128-bit vectorised persistent kernel. The
+ * C = A + scalar * B, on the 128-bit vectorised kernel (one vector per
+ * thread, blocks in address order). The
  * scalar is the reference's 0.5 unless GPL_TRIAD_SCALAR is set (the
  * measured configuration uses 3.0); GPL_TRIAD_KERNEL=bulk selects the
  * TMA-bulk-staged variant.
