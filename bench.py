@@ -562,6 +562,12 @@ def bench_gemm(args, dist: Dist) -> dict:
     achieved = flops / kernel_s / 1e12
     value = dist.world * flops * args.steps / (ms_max / 1e3) / 1e12
     peak, peak_source = NOMINAL_TFLOPS[w], "nominal dense"
+    if w in ("bf16", "f16"):
+        # The pool's measured dense BF16 rate (cuBLAS, burst) is the roofline
+        # for the 16-bit kinds; the other kinds have no measured figure.
+        pk = measured_peaks()
+        peak = pk["bf16_tflops"]
+        peak_source = f"{pk['_source']} bf16_tflops (burst cuBLAS BF16 8192^3); nominal {NOMINAL_TFLOPS[w]:.0f}"
     scalar_ffma = None
     if w == "sgemm":
         # Scalar FFMA alone stays well below the nominal FP32 rate on B200
