@@ -77,6 +77,8 @@ def parse_args():
     ap.add_argument("--fabric", choices=["nccl", "gplk"], default="nccl",
                     help="powervirus fabric step: NCCL all_reduce, or gplk_fabric_allreduce_bf16 over NVLink peers")
     ap.add_argument("--fabric-mib", type=int, default=256, help="fabric allreduce size (BF16), MiB")
+    ap.add_argument("--gemm-n", type=int, default=0,
+                    help="M = N = K of the tensor-core GEMM workloads (0: 8192, 16384 for nvfp4)")
     ap.add_argument("--sgemm-n", type=int, default=1024,
                     help="sgemm workload size M = N = K (1024 is the parity configuration; the rung's --size "
                          "default is 4096)")
@@ -488,7 +490,7 @@ def bench_gemm(args, dist: Dist) -> dict:
         dtype, workload = "f32", f"FP32 SGEMM C = A*B row-major, M=N=K={n}, U[-1,1)"
         launches_per_step = 2
     elif w in NN_GEMMS:
-        n = 8192
+        n = args.gemm_n or 8192
         if w == "i8":
             A = torch.randint(-128, 128, (n, n), dtype=torch.int8, device=dev, generator=g)
             B = torch.randint(-128, 128, (n, n), dtype=torch.int8, device=dev, generator=g)
@@ -505,7 +507,7 @@ def bench_gemm(args, dist: Dist) -> dict:
         dtype, workload = NN_GEMMS[w]
         launches_per_step = 1
     else:
-        n = 8192 if w == "fp8" else 16384
+        n = args.gemm_n or (8192 if w == "fp8" else 16384)
         if w == "fp8":
             A = (torch.randn(n, n, device=dev, generator=g) * 32).clamp(-448, 448).to(torch.float8_e4m3fn).view(torch.uint8)
             B = (torch.randn(n, n, device=dev, generator=g) * 32).clamp(-448, 448).to(torch.float8_e4m3fn).view(torch.uint8)
@@ -584,7 +586,7 @@ def bench_gemm(args, dist: Dist) -> dict:
                    "parallelism": f"replicas x{dist.world}"},
         "roofline": {"bound": "tensor" if w != "sgemm" else "fp32-simt", "achieved": round(achieved, 1),
                      "peak": round(peak, 1), "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
-                     "traffic": NCU_TRAFFIC.get(w) if (w != "sgemm" or n == 1024) else None,
+                     "traffic": NCU_TRAFFIC.get(w) if n == {"sgemm": 1024, "nvfp4": 16384}.get(w, 8192) else None,
                      "peak_source": peak_source,
                      **({"scalar_ffma_measured": scalar_ffma} if scalar_ffma is not None else {})},
         "clocks": sampler.summary(),
