@@ -36,16 +36,16 @@ TRIAD_N = 1 << 30
 TRIAD_S = 3.0
 TRIAD_BYTES = 12 * TRIAD_N  # read b, read c, write a (runner/src/workload_util.c:43-47)
 
-# dram__bytes_read.sum + dram__bytes_write.sum per launch from ncu captures
-# (profiles/*.md, scaled to the full launch where the capture was smaller).
+# dram__bytes_read.sum + dram__bytes_write.sum per launch from one ncu capture
+# of each kernel, scaled to the full launch where the capture was smaller.
 NCU_TRAFFIC = {
-    "memstream_vec4": 12.58e9,  # profiles/memstream_triad_2p30.md: 8 x 1.573 GB (3 x 2^27 capture)
-    "memstream_bulk": 12.58e9,  # profiles/memstream_triad_2p30.md: 8 x 1.572 GB (3 x 2^27 capture)
-    "sgemm": 8.4e6,             # profiles/sgemm_f32_1024.md
-    "fp8": 339.8e6,             # profiles/gemm_fp8_8192.md (odd raster groups walking N backwards)
-    "nvfp4": 1343.6e6,          # profiles/gemm_nvfp4_16384.md
-    "bf16": 1149.9e6,           # profiles/gemm_nn_bf16_i8_8192.md
-    "tf32": 2452.5e6,           # profiles/gemm_nn_bf16_i8_8192.md
+    "memstream_vec4": 12.58e9,  # 8 x 1.573 GB (3 x 2^27 capture)
+    "memstream_bulk": 12.58e9,  # 8 x 1.572 GB (3 x 2^27 capture)
+    "sgemm": 8.4e6,             # 1024^3
+    "fp8": 339.8e6,             # 8192^3 (odd raster groups walking N backwards)
+    "nvfp4": 1343.6e6,          # 16384^3
+    "bf16": 1149.9e6,           # 8192^3
+    "tf32": 2452.5e6,           # 8192^3
 }
 
 NOMINAL_TFLOPS = {"fp8": 4500.0, "nvfp4": 9000.0, "sgemm": 148 * 128 * 2 * 1.965e9 / 1e12,
@@ -86,6 +86,12 @@ def parse_args():
     ap.add_argument("--budget-us", type=float, default=1000.0, help="powervirus launch time box")
     ap.add_argument("--duty-on-ms", type=float, default=100.0)
     ap.add_argument("--duty-off-ms", type=float, default=100.0)
+    ap.add_argument("--no-rungs", action="store_true",
+                    help="memstream at N=1: skip the FP8 / NVFP4 GEMM and power rungs added to the line")
+    ap.add_argument("--rung-seconds", type=float, default=1.5,
+                    help="sustained run per GEMM rung arm (the power rung runs twice as long)")
+    ap.add_argument("--no-fabric-check", action="store_true",
+                    help="memstream at N>1: skip the fabric step's parity check and timing added to the line")
     ap.add_argument("--elements", type=int, default=TRIAD_N,
                     help="memstream array length (smaller cases are for profiling only)")
     return ap.parse_args()
@@ -229,6 +235,17 @@ class ClockSampler:
                 except Exception:
                     pass
 
+    def power_stats(self, skip_s: float = 0.0) -> dict:
+        """Mean and percentiles of the power samples taken more than skip_s
+        after the first sample (the controller settles in the first ~0.3 s)."""
+        if not self.samples:
+            return {"avg_w": None, "samples": 0}
+        t0 = self.samples[0][0]
+        w = sorted(s[3] for s in self.samples if s[0] - t0 >= skip_s) or sorted(s[3] for s in self.samples)
+        pct = lambda q: w[min(len(w) - 1, int(q * (len(w) - 1)))]  # noqa: E731
+        return {"avg_w": round(sum(w) / len(w), 1), "p5_w": round(pct(0.05), 1), "p95_w": round(pct(0.95), 1),
+                "max_w": round(w[-1], 1), "samples": len(w), "limit_w": self.limit_w}
+
     def summary(self) -> dict:
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": self.max_sm, "reasons": [], "samples": 0}
@@ -259,6 +276,15 @@ def measured_peaks() -> dict:
 
 # ------------------------------------------------------------ CPU baseline (oracle port)
 
+def host_threads() -> int:
+    """Every core this process may run on. Passed to the host loops
+    explicitly, so torchrun's OMP_NUM_THREADS=1 does not shrink them."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_triad_gbps(seconds: float, n: int = 1 << 28, threads: int = 0) -> dict:
     """The host triad a = fmaf(s, c, b) (the oracle's restatement of the
     triad) over n elements, repeated for about `seconds`, all cores."""
@@ -269,7 +295,7 @@ def cpu_triad_gbps(seconds: float, n: int = 1 << 28, threads: int = 0) -> dict:
     b = oracle.uniform_f32(n, seed=101)
     c = oracle.uniform_f32(n, seed=202)
     a = np.empty_like(b)
-    nthreads = threads or oracle.max_threads()
+    nthreads = threads or host_threads()
     oracle.triad_into(a, b, c, TRIAD_S, nthreads)  # first touch
     reps, t0 = 0, time.perf_counter()
     while True:
@@ -292,7 +318,7 @@ def cpu_sgemm_tflops(n: int, seconds: float) -> dict:
 
     A = oracle.uniform_f32(n * n, seed=0, lo=-1.0, hi=1.0).reshape(n, n)
     B = oracle.uniform_f32(n * n, seed=1, lo=-1.0, hi=1.0).reshape(n, n)
-    nthreads = oracle.max_threads()
+    nthreads = host_threads()
     # Whole problem up to 1024^3; above that a row slab of about 2 GFLOP.
     slab = n if n <= 1024 else max(16, (1 << 30) // (n * n))
     As = A if slab == n else A[:slab].copy()
@@ -631,6 +657,319 @@ def fma_peak_tflops(dev, stream, inner: int = 10000, launches: int = 60) -> dict
     return out
 
 
+# ------------------------------------------------------------ the metric's other rungs (N = 1 line)
+
+def _sustained(fn, stream, dev, seconds: float, skip_s: float = 0.3) -> dict:
+    """Run fn back to back for about `seconds` (count fixed from a short
+    timing first), CUDA events around the whole run on `stream`, NVML
+    clocks and power sampled meanwhile."""
+    import torch
+
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(5):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    reps = max(5, int(seconds / max(e0.elapsed_time(e1) / 5e3, 1e-6)))
+    sampler = ClockSampler(dev.index if dev.index is not None else 0, period_s=0.02)
+    sampler.start()
+    e0.record(stream)
+    for _ in range(reps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    sampler.stop()
+    return {"reps": reps, "s": e0.elapsed_time(e1) / 1e3, "clocks": sampler.summary(),
+            "power": sampler.power_stats(skip_s)}
+
+
+def _energy(tflops: float, run: dict) -> dict:
+    clk, pw = run["clocks"], run["power"]
+    out = {"sm_mhz": clk.get("sm_mhz"), "reasons": clk.get("reasons"), "avg_w": pw.get("avg_w")}
+    if clk.get("sm_mhz"):
+        out["tflops_per_mhz"] = round(tflops / clk["sm_mhz"], 4)
+    if pw.get("avg_w"):
+        out["j_per_tflop"] = round(pw["avg_w"] / tflops, 4)
+    return out
+
+
+def _gemm_e2e(inputs, output, launch, flops: float, stream, steps: int = 3) -> dict:
+    """The GEMM through the C ABI with host operands: every step copies the
+    inputs from pinned host memory, runs the GEMM and copies D back, all on
+    one stream between CUDA events."""
+    import torch
+
+    hin = [(t.cpu().pin_memory(), t) for t in inputs]
+    hout = torch.empty(output.shape, dtype=output.dtype, pin_memory=True)
+
+    def step():
+        for h, d in hin:
+            d.copy_(h, non_blocking=True)
+        launch()
+        hout.copy_(output, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    s = e0.elapsed_time(e1) / 1e3
+    return {"value": round(flops * steps / s / 1e12, 2), "unit": "TFLOP/s",
+            "h2d_bytes_per_step": int(sum(t.numel() * t.element_size() for t in inputs)),
+            "d2h_bytes_per_step": int(output.numel() * output.element_size()), "steps": steps,
+            "note": "pinned host operands -> device, GEMM, D -> pinned host, on one stream, every step"}
+
+
+def _rel_frob(a, b) -> float:
+    a, b = a.float(), b.float()
+    return float((a - b).norm() / b.norm().clamp_min(1e-30))
+
+
+def rung_gemm(kind: str, dev, stream, seconds: float) -> dict:
+    """FP8 E4M3 8192^3 or NVFP4 16384^3 on N(0,1) operands quantised as the
+    rung configuration states (gplk.operands), through the C ABI; the same
+    operands through cuBLASLt (torch's scaled matmul) on the same GPU beside
+    it; and the GEMM end to end with host operands."""
+    import torch
+    import torch.nn.functional as F
+    import gplk
+    from gplk import operands as O
+
+    n = 8192 if kind == "fp8" else 16384
+    flops = 2.0 * n ** 3
+    xa = O.normal(n, n, 31, dev)
+    if kind == "fp8":
+        qa, sa = O.quantize_fp8(xa)
+        del xa
+        xb = O.normal(n, n, 32, dev)
+        qb, sb = O.quantize_fp8(xb)
+        del xb
+        scale_a = torch.tensor([sa], device=dev)
+        scale_b = torch.tensor([sb], device=dev)
+        D = torch.empty(n, n, dtype=torch.bfloat16, device=dev)  # column-major M x N as (N, M)
+
+        def ours():
+            gplk.gemm_fp8_tn(qa, qb, D, scale_a, scale_b, stream=stream)
+
+        fa, fb = qa.view(torch.float8_e4m3fn), qb.view(torch.float8_e4m3fn)
+
+        def library():
+            return torch._scaled_mm(fa, fb.t(), scale_a=scale_a, scale_b=scale_b, out_dtype=torch.bfloat16)
+
+        lib_name = "cuBLASLt FP8 TN via torch._scaled_mm (per-tensor scales, BF16 out)"
+        inputs = [qa, qb]
+        workload = "FP8 E4M3 TN GEMM M=N=K=8192, N(0,1) operands, per-tensor amax/448 scales, FP32 acc, BF16 out"
+        peak = NOMINAL_TFLOPS["fp8"]
+    else:
+        qa, sfa, ga = O.quantize_nvfp4(xa)
+        del xa
+        xb = O.normal(n, n, 32, dev)
+        qb, sfb, gb = O.quantize_nvfp4(xb)
+        del xb
+        alpha = torch.tensor([ga * gb], device=dev)
+        D = torch.empty(n, n, dtype=torch.bfloat16, device=dev)
+
+        def ours():
+            gplk.gemm_nvfp4_tn(qa, qb, sfa, sfb, D, n, alpha, stream=stream)
+
+        fa = qa.view(torch.float4_e2m1fn_x2)
+        fb = qb.view(torch.float4_e2m1fn_x2)
+        ssa = sfa.view(torch.float8_e4m3fn).view(n, n // 16)
+        ssb = sfb.view(torch.float8_e4m3fn).view(n // 16, n)
+        gat, gbt = torch.tensor([ga], device=dev), torch.tensor([gb], device=dev)
+
+        def library():
+            return F.scaled_mm(fa, fb.t(), [ssa, gat], [F.ScalingType.BlockWise1x16, F.ScalingType.TensorWise],
+                               [ssb, gbt], [F.ScalingType.BlockWise1x16, F.ScalingType.TensorWise],
+                               swizzle_a=[F.SwizzleType.SWIZZLE_32_4_4], swizzle_b=[F.SwizzleType.SWIZZLE_32_4_4],
+                               output_dtype=torch.bfloat16)
+
+        lib_name = "cuBLASLt NVFP4 (VEC16 UE4M3 block scales + per-tensor scales) via torch scaled_mm"
+        inputs = [qa, qb, sfa, sfb]
+        workload = ("NVFP4 E2M1 TN GEMM M=N=K=16384, N(0,1) operands, UE4M3 per-16 block scales + per-tensor "
+                    "FP32 scale, FP32 acc, BF16 out")
+        peak = NOMINAL_TFLOPS["nvfp4"]
+
+    run = _sustained(ours, stream, dev, seconds)
+    tflops = flops * run["reps"] / run["s"] / 1e12
+    out = {"metric": f"{kind} GEMM TFLOP/s", "value": round(tflops, 1), "unit": "TFLOP/s", "dtype":
+           "e4m3" if kind == "fp8" else "e2m1", "config": {"workload": workload, "size": n,
+                                                             "l2": "operands larger than L2"},
+           "launches": run["reps"], "seconds": round(run["s"], 3),
+           "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s",
+                        "frac": round(tflops / peak, 4), "peak_source": "nominal dense",
+                        "traffic": NCU_TRAFFIC.get(kind)},
+           "clocks": run["clocks"], "energy": _energy(tflops, run)}
+    lib_out = {"impl": lib_name}
+    try:
+        ref = library()
+        torch.cuda.synchronize(dev)
+        ours()
+        torch.cuda.synchronize(dev)
+        lib_out["rel_frob_vs_ours"] = round(_rel_frob(D.view(n, n).t(), ref), 6)
+        del ref
+        lrun = _sustained(library, stream, dev, seconds)
+        ltf = flops * lrun["reps"] / lrun["s"] / 1e12
+        lib_out.update({"value": round(ltf, 1), "unit": "TFLOP/s", "clocks": lrun["clocks"],
+                        "energy": _energy(ltf, lrun), "ours_over_library": round(tflops / ltf, 4)})
+    except Exception as exc:  # the library's kernel for this format may be missing from this torch build
+        lib_out["unavailable"] = f"{type(exc).__name__}: {str(exc).splitlines()[0][:200]}"
+    out["library"] = lib_out
+    out["e2e"] = _gemm_e2e(inputs, D, ours, flops, stream)
+    code, site = gplk.status_read()
+    if code != 0:
+        raise RuntimeError(f"device status {code} at {site:#x}")
+    return out
+
+
+def rung_power(dev, stream, seconds: float, mix=(4, 1, 2), budget_us: float = 1000.0) -> dict:
+    """Sustained power of the powervirus kernel (time-boxed launches back to
+    back) as a percentage of the enforced limit, beside the reference's
+    strongest library rung on the same GPU: cuBLASLt FP8 8192^3 GEMMs back
+    to back on operands filled with 0x38 (E4M3 1.0), as the reference's
+    gpl_lt_init fills them."""
+    import torch
+    import gplk
+
+    weights = list(mix) + [0] * (8 - len(mix))
+    m, counts = gplk.pv_role_map(weights)
+    role_map = torch.tensor(m, dtype=torch.uint8, device=dev)
+    buf = torch.full((2 << 30,), 0x3C, dtype=torch.uint8, device=dev)
+    sink = torch.zeros(1 + 1024, dtype=torch.float32, device=dev)
+    cfg = gplk.PvCfg(role_map=role_map.data_ptr(), stream_buf=buf.data_ptr(), stream_bytes=buf.numel(),
+                     sink=sink.data_ptr(), blocks=0, inner=256, budget_ns=int(budget_us * 1e3))
+    idle = ClockSampler(dev.index if dev.index is not None else 0, period_s=0.02)
+    torch.cuda.synchronize(dev)
+    time.sleep(0.3)
+    idle.start()
+    time.sleep(0.5)
+    idle.stop()
+    idle_w = idle.power_stats().get("avg_w")
+    run = _sustained(lambda: gplk.powervirus_launch(cfg, stream=stream), stream, dev, seconds, skip_s=0.5)
+    limit = run["power"].get("limit_w") or 1000.0
+    lvl = run["power"].get("avg_w") or 0.0
+    out = {"metric": "powervirus sustained power % of enforced limit", "value": round(100.0 * lvl / limit, 2),
+           "unit": "%", "config": {"workload": "powervirus, continuous time-boxed launches: in-kernel tcgen05 FP8 + "
+                                               "FFMA chains + TMA-bulk HBM streaming (2 GiB)",
+                                   "mix_tensor_fma_dram": list(mix), "warps_per_64": counts,
+                                   "launch_budget_us": budget_us},
+           "launches": run["reps"], "seconds": round(run["s"], 3), "power": run["power"], "clocks": run["clocks"],
+           "idle_w": idle_w, "swing_w": round(lvl - idle_w, 1) if idle_w else None, "enforced_limit_w": limit}
+    del buf
+    code, site = gplk.status_read()
+    if code != 0:
+        raise RuntimeError(f"device status {code} at {site:#x}")
+    lib = {"impl": "cuBLASLt FP8 8192^3 TN GEMMs via torch._scaled_mm on 0x38 operands "
+                   "(the reference's gpl_lt rung, tensor-only)"}
+    try:
+        n = 8192
+        a = torch.full((n, n), 0x38, dtype=torch.uint8, device=dev).view(torch.float8_e4m3fn)
+        b = torch.full((n, n), 0x38, dtype=torch.uint8, device=dev).view(torch.float8_e4m3fn)
+        one = torch.ones(1, device=dev)
+        lrun = _sustained(lambda: torch._scaled_mm(a, b.t(), scale_a=one, scale_b=one, out_dtype=torch.bfloat16),
+                          stream, dev, seconds, skip_s=0.5)
+        llvl = lrun["power"].get("avg_w") or 0.0
+        lib.update({"value": round(100.0 * llvl / limit, 2), "unit": "%", "power": lrun["power"],
+                    "clocks": lrun["clocks"]})
+        out["ours_minus_library_pct_points"] = round(out["value"] - lib["value"], 2)
+    except Exception as exc:
+        lib["unavailable"] = f"{type(exc).__name__}: {str(exc).splitlines()[0][:200]}"
+    out["library"] = lib
+    return out
+
+
+def bench_rungs(args, dist: Dist) -> dict:
+    """The metric's GEMM and power rungs, on this rank's GPU."""
+    import torch
+
+    dev = torch.device("cuda", dist.local)
+    stream = torch.cuda.current_stream(dev)
+    out = {}
+    for kind in ("fp8", "nvfp4"):
+        out[kind] = rung_gemm(kind, dev, stream, args.rung_seconds)
+        torch.cuda.empty_cache()
+    out["powervirus"] = rung_power(dev, stream, 2.0 * args.rung_seconds)
+    torch.cuda.empty_cache()
+    return out
+
+
+# ------------------------------------------------------------ fabric step beside the replicas (N > 1)
+
+def fabric_check(dist: Dist, mib: int, steps: int, warmup: int) -> dict:
+    """The powervirus cycle's fabric step on the replicas' GPUs: one
+    gplk_fabric_allreduce_bf16 of `mib` MiB checked bit for bit against the
+    same sum restated with torch (every rank's input gathered, added in FP32
+    in rank order, rounded once to BF16), then timed beside NCCL's
+    all_reduce on a buffer of the same size. Every rank takes the same
+    collective steps; the verdict is agreed over all ranks."""
+    import torch
+    import gplk
+    from gplk import rung
+    from gplk.fabric import Fabric
+
+    dev = torch.device("cuda", dist.local)
+    count = (mib << 20) // 2
+    fab = Fabric(dist.pg.group.WORLD, count * 2)
+    buf = fab.tensor(count)
+    g = torch.Generator(device=dev)
+    g.manual_seed(11 + dist.rank)
+    x = torch.randn(count, device=dev, generator=g).to(torch.bfloat16)
+    parts = [torch.empty_like(x) for _ in range(dist.world)]
+    dist.pg.all_gather(parts, x)
+    want = parts[0].float()
+    for p in parts[1:]:
+        want = want + p.float()
+    want = want.to(torch.bfloat16)
+    del parts
+    stream = torch.cuda.current_stream(dev)
+    buf.copy_(x)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    fab.allreduce_bf16(count, stream=stream)
+    torch.cuda.synchronize(dev)
+    same = bool(torch.equal(buf.view(torch.int16), want.view(torch.int16)))
+    bitexact = dist.sum(1.0 if same else 0.0) == dist.world
+    del want
+    other = x.clone()
+    res = {}
+    for name, fn in (("gplk", lambda: fab.allreduce_bf16(count, stream=stream)),
+                     ("nccl", lambda: dist.pg.all_reduce(other))):
+        buf.copy_(x)
+        other.copy_(x)
+        for _ in range(max(warmup, 3)):
+            fn()
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        res[name] = dist.max(e0.elapsed_time(e1)) / steps
+    code, site = gplk.status_read()
+    dist.barrier()
+    fab.close()
+    status_ok = dist.sum(1.0 if code == 0 else 0.0) == dist.world
+    nbytes = count * 2
+    bus = {k: rung.allreduce_busbw_gbs(nbytes, v / 1e3, dist.world) for k, v in res.items()}
+    return {"impl": "gplk_fabric_allreduce_bf16 (NVLink peer loads/stores, no multicast)",
+            "bytes": nbytes, "bitexact": bitexact, "status_ok": status_ok,
+            "check": "every rank's seeded N(0,1) BF16 input gathered, summed in FP32 in rank order, rounded once",
+            "ms_gplk": round(res["gplk"], 4), "busbw_gplk": round(bus["gplk"], 1),
+            "ms_nccl": round(res["nccl"], 4), "busbw_nccl": round(bus["nccl"], 1),
+            "gplk_over_nccl": round(res["nccl"] / res["gplk"], 4), "steps": steps}
+
+
 # ------------------------------------------------------------ powervirus rung
 
 def node_power_summary(mon, on_ms: float, off_ms: float, phase: str) -> dict | None:
@@ -807,57 +1146,26 @@ def bench_fabric(args, dist: Dist) -> dict:
     (value) against NCCL's all_reduce (reported beside it), CUDA events, max
     over ranks. Bus bandwidth follows NCCL's convention 2 (N-1)/N x bytes / t."""
     import torch
-    from gplk import rung
-    from gplk.fabric import Fabric
 
     if dist.world < 2:
         return {"metric": "fabric allreduce bus bandwidth", "unavailable": "needs 2 or more GPUs (torchrun)",
                 "n_gpus": dist.world}
-    dev = torch.device("cuda", dist.local)
-    torch.cuda.set_device(dev)
-    count = (args.fabric_mib << 20) // 2
-    fab = Fabric(dist.pg.group.WORLD, count * 2)
-    buf = fab.tensor(count)
-    g = torch.Generator(device=dev)
-    g.manual_seed(11 + dist.rank)
-    buf.copy_(torch.randn(count, device=dev, generator=g).to(torch.bfloat16))
-    ref = buf.clone()
-    stream = torch.cuda.current_stream(dev)
-    res = {}
-    for name, fn in (("gplk", lambda: fab.allreduce_bf16(count, stream=stream)),
-                     ("nccl", lambda: dist.pg.all_reduce(ref))):
-        for _ in range(max(args.warmup, 3)):
-            fn()
-        torch.cuda.synchronize(dev)
-        dist.barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(args.steps):
-            fn()
-        e1.record(stream)
-        torch.cuda.synchronize(dev)
-        dist.barrier()
-        res[name] = dist.max(e0.elapsed_time(e1)) / args.steps
-    import gplk
-
-    code, site = gplk.status_read()
-    dist.barrier()
-    fab.close()
-    if code != 0:
-        raise RuntimeError(f"device status {code} at {site:#x}")
-    nbytes = count * 2
-    bus = {k: rung.allreduce_busbw_gbs(nbytes, v / 1e3, dist.world) for k, v in res.items()}
+    torch.cuda.set_device(torch.device("cuda", dist.local))
+    f = fabric_check(dist, args.fabric_mib, args.steps, args.warmup)
+    if not f["status_ok"]:
+        raise RuntimeError("fabric step recorded a device status")
     link = 770.0  # measured peer copy GB/s per direction per GPU on this pool
     return {
-        "metric": "fabric allreduce bus bandwidth", "value": round(bus["gplk"], 1), "unit": "GB/s",
+        "metric": "fabric allreduce bus bandwidth", "value": f["busbw_gplk"], "unit": "GB/s",
         "n_gpus": dist.world, "steps": args.steps, "warmup": max(args.warmup, 3),
-        "ms_per_step": round(res["gplk"], 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "ms_per_step": f["ms_gplk"], "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic N(0,1) BF16, seeded per rank",
         "config": {"workload": f"in-place BF16 sum allreduce of {args.fabric_mib} MiB per rank, one process per GPU",
                    "parallelism": f"allreduce x{dist.world}"},
-        "nccl": {"ms_per_step": round(res["nccl"], 4), "busbw_gbs": round(bus["nccl"], 1)},
-        "roofline": {"bound": "nvlink", "achieved": round(bus["gplk"], 1), "peak": link, "unit": "GB/s",
-                     "frac": round(bus["gplk"] / link, 4), "traffic": None,
+        "nccl": {"ms_per_step": f["ms_nccl"], "busbw_gbs": f["busbw_nccl"]},
+        "fabric": f,
+        "roofline": {"bound": "nvlink", "achieved": f["busbw_gplk"], "peak": link, "unit": "GB/s",
+                     "frac": round(f["busbw_gplk"] / link, 4), "traffic": None,
                      "peak_source": "measured peer copy per direction (pool figure)"},
         "gpu_launches": args.steps,
     }
@@ -891,7 +1199,7 @@ def bench_reference(args, dist: Dist) -> dict | None:
     b = oracle.uniform_f32(n, seed=101)
     c = oracle.uniform_f32(n, seed=202)
     a = np.empty_like(b)
-    th = oracle.max_threads()
+    th = host_threads()
     for _ in range(max(args.warmup, 1)):
         oracle.triad_into(a, b, c, TRIAD_S, th)
     t0 = time.perf_counter()
@@ -906,7 +1214,9 @@ def bench_reference(args, dist: Dist) -> dict | None:
         "ms_per_step": round(el * 1e3 / args.steps, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic: b, c ~ U[0,1) seeded, s = 3.0",
         "config": {"workload": "memstream STREAM triad a = b + 3.0*c, FP32, 3 x 2^30 elements (4 GiB each)",
-                   "sampled_elements_per_step": n},
+                   "sampled_elements_per_step": n,
+                   "scope": f"one host: the node's whole CPU triad throughput on {th} cores, whatever the number "
+                            "of GPUs (rank 0 runs it; the value is per byte, a 3 x 2^28 sample of the workload)"},
         "cpu_baseline": {"value": round(value, 2), "unit": "GB/s", "cores": th, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(value, 2), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -936,8 +1246,13 @@ def main():
             line = bench_fabric(args, dist)
         else:
             line = bench_powervirus(args, dist)
-        if dist.rank == 0 and dist.world == 1 and not args.no_cpu and args.workload == "memstream":
+        if args.workload == "memstream" and dist.world == 1 and not args.no_rungs:
+            line["rungs"] = bench_rungs(args, dist)
+        if args.workload == "memstream" and dist.world > 1 and not args.no_fabric_check:
+            line["fabric"] = fabric_check(dist, args.fabric_mib, steps=10, warmup=3)
+        if dist.rank == 0 and not args.no_cpu and args.workload == "memstream":
             line["cpu_baseline"] = cpu_triad_gbps(args.cpu_seconds)
+        dist.barrier()  # the other ranks wait for rank 0's host baseline
         if dist.rank == 0 and dist.world == 1 and not args.no_cpu and args.workload == "sgemm":
             line["cpu_baseline"] = cpu_sgemm_tflops(args.sgemm_n, min(args.cpu_seconds, 10.0))
         if dist.rank == 0:

@@ -29,4 +29,7 @@ nvcc $GEN -O2 -Xcompiler -fPIC -I"$SRC" -c "$SRC/gemm_lt.cu" -o "$TMP/gemm_lt.o"
 nvcc $GEN -O2 -Xcompiler -fPIC -I"$SRC" -c "$HERE/ref_shim.cu" -o "$TMP/ref_shim.o"
 gcc -std=gnu11 -O2 -fPIC -I"$SRC" -I/usr/local/cuda/include -c "$HERE/ref_gemm_shim.c" -o "$TMP/ref_gemm_shim.o"
 nvcc $GEN -shared -o "$OUT/libgpl_ref.so" "$TMP"/*.o -lcublasLt -lcublas
+# Record where the reference tree was found, for the tests that read its
+# schema and host sources (they skip where this file names no tree).
+printf '%s\n' "$REF" > "$OUT/reference_root"
 echo "ref_build: wrote $OUT/libgpl_ref.so"

@@ -17,6 +17,22 @@ for p in (PKG, REPO / "oracle", REPO):
         sys.path.insert(0, str(p))
 
 
+def reference_root() -> Path | None:
+    """The gpu-power-lab source tree the parity recipes were built from:
+    $GPL_REFERENCE_ROOT, else the path oracle/ref_build.sh recorded in
+    oracle/_ref/reference_root. None when neither names an existing tree
+    (the tests that read the reference's schema or host sources then skip)."""
+    import os
+
+    cand = os.environ.get("GPL_REFERENCE_ROOT")
+    rec = REPO / "oracle" / "_ref" / "reference_root"
+    if not cand and rec.exists():
+        cand = rec.read_text().strip()
+    if cand and Path(cand).is_dir():
+        return Path(cand)
+    return None
+
+
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
 

@@ -25,7 +25,10 @@ import pytest
 from gplk import summary as S
 
 REPO = Path(__file__).resolve().parent.parent
-REF_SRC = Path("/root/reference/runner/src")
+from conftest import reference_root
+
+_REF = reference_root()
+REF_SRC = (_REF / "runner" / "src") if _REF else Path("/nonexistent")
 DROP = REPO / "gpu-power-lab_b200" / "runner"
 CUDA = Path("/usr/local/cuda")
 
@@ -126,8 +129,8 @@ def test_strict_mode(case, harnesses, tmp_path):
 
 
 def test_strict_output_meets_reference_schema(harnesses, tmp_path):
-    ref_schema = Path("/root/reference/schema/rung-summary.schema.json")
-    if not ref_schema.exists():
+    ref_schema = (_REF / "schema" / "rung-summary.schema.json") if _REF else None
+    if ref_schema is None or not ref_schema.exists():
         pytest.skip("reference schema not present")
     import jsonschema
 

@@ -20,7 +20,10 @@ import pytest
 from gplk import summary as S
 
 GOLDEN = Path(__file__).resolve().parent / "golden" / "summaries"
-REF_SCHEMA = Path("/root/reference/schema/rung-summary.schema.json")
+from conftest import reference_root
+
+_REF = reference_root()
+REF_SCHEMA = (_REF / "schema" / "rung-summary.schema.json") if _REF else Path("/nonexistent")
 
 
 def _doc() -> dict:
