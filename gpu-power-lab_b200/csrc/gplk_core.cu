@@ -157,7 +157,7 @@ extern "C" const char* gplk_status_string(int status) {
     }
 }
 
-extern "C" int gplk_abi_version(void) { return 2; }
+extern "C" int gplk_abi_version(void) { return 3; }
 
 extern "C" int gplk_status_read(int* code, int* site, int clear) {
     if (cudaDeviceSynchronize() != cudaSuccess) return GPLK_STATUS_CUDA_ERROR;

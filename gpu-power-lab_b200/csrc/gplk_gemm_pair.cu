@@ -11,8 +11,11 @@
 //         the last four in the layout of the reference's cublasGemmEx rung
 //         (runner/src/workload_gemm.c:44-79 maps them, :155-163 calls them):
 //         all matrices column-major, C = A * B with no transposes, alpha 1,
-//         beta 0. Column-major A (M x K) has M contiguous, so the MMA reads
-//         it MN-major; column-major B (K x N) is K-major. The reference
+//         beta 0 -- or beta 1 (C = A * B + C, the powervirus tensor stream's
+//         call, runner/src/workload_powervirus.cu:363-380): the epilogue
+//         then reads the old C element, adds it to the FP32 / S32 sum and
+//         rounds once. Column-major A (M x K) has M contiguous, so the MMA
+//         reads it MN-major; column-major B (K x N) is K-major. The reference
 //         computes FP16 with CUBLAS_COMPUTE_16F; here FP16 accumulates in
 //         FP32 (at least as accurate) and rounds once to FP16.
 // D is always M x N column-major.
@@ -142,6 +145,25 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
     return r;
 }
 
+// acc + old for beta = 1, in the accumulator's type: FP32 add (the old
+// BF16 / FP16 value widened exactly) or wrapping S32 add. The sum is then
+// rounded once to the output type by the epilogue, as cuBLAS computes
+// alpha * acc + beta * C with alpha = beta = 1.
+template <Out OUT>
+__device__ __forceinline__ uint32_t add_old(uint32_t acc_bits, uint32_t old) {
+    if constexpr (OUT == Out::S32) {
+        return (uint32_t)((int32_t)acc_bits + (int32_t)old);
+    } else if constexpr (OUT == Out::F32) {
+        return __float_as_uint(__fadd_rn(__uint_as_float(acc_bits), __uint_as_float(old)));
+    } else if constexpr (OUT == Out::BF16) {
+        return __float_as_uint(__fadd_rn(__uint_as_float(acc_bits), __uint_as_float(old << 16)));
+    } else {
+        float h;
+        asm("cvt.f32.f16 %0, %1;" : "=f"(h) : "h"((unsigned short)old));
+        return __float_as_uint(__fadd_rn(__uint_as_float(acc_bits), h));
+    }
+}
+
 struct Params {
     void* D;
     const float* scale_a;  // FP8: per-tensor scales (device pointers)
@@ -150,6 +172,7 @@ struct Params {
     int m_tiles, n_tiles, k_stages;
     int group_m;    // raster group along M (pair tiles)
     int tma_store;  // stage the epilogue through shared memory and TMA-store it
+    int accumulate; // beta = 1: D = A * B + D (D read before it is written)
 };
 
 struct __align__(1024) Smem {
@@ -368,8 +391,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll 1
             for (int c = 0; c < C::kChunks; ++c) {
                 uint32_t r[CC];
+                // beta = 1: this thread's row of the chunk's CC columns of the
+                // old D, loaded before the accumulator is read so the loads'
+                // latency overlaps the TMEM read (a warp reads 32 consecutive
+                // rows of one column: 64 or 128 contiguous bytes).
+                uint32_t old[CC];
+                if (p.accumulate) {
+                    const bool row_ok = m < p.M;
+#pragma unroll
+                    for (int j = 0; j < CC; ++j) {
+                        const int n = n_base + CC * c + j;
+                        old[j] = 0u;
+                        if (row_ok && n < p.N) {
+                            const size_t off = (size_t)n * (size_t)p.M + (size_t)m;
+                            if constexpr (C::kOutBytes == 2)
+                                old[j] = (uint32_t)__ldcs(static_cast<const uint16_t*>(p.D) + off);
+                            else
+                                old[j] = __ldcs(static_cast<const uint32_t*>(p.D) + off);
+                        }
+                    }
+                }
                 tmem_ld_cols<CC>(t_addr + (uint32_t)(CC * c), r);
                 tmem_ld_wait();
+                if (p.accumulate) {
+#pragma unroll
+                    for (int j = 0; j < CC; ++j) r[j] = add_old<C::kOut>(r[j], old[j]);
+                }
                 if (c == C::kChunks - 1) {  // the accumulator is in registers: release it
                     tc_fence_before();
                     __syncwarp();
@@ -448,7 +495,7 @@ static int encode_operand(CUtensorMap* map, const void* base, uint64_t row_bytes
 
 template <class C>
 static int launch(const void* A, const void* B, void* D, int M, int N, int K, cudaStream_t stream,
-                  const float* scale_a = nullptr, const float* scale_b = nullptr) {
+                  const float* scale_a = nullptr, const float* scale_b = nullptr, bool accumulate = false) {
     DeviceInfo d;
     int st = require_sm100(&d);
     if (st != GPLK_STATUS_OK) return st;
@@ -505,6 +552,7 @@ static int launch(const void* A, const void* B, void* D, int M, int N, int K, cu
     p.n_tiles = (N + 255) / 256;
     p.scale_a = scale_a;
     p.scale_b = scale_b;
+    p.accumulate = accumulate ? 1 : 0;
     {
         // As many pair-tiles per raster group as keep the group's A panels
         // within the budget, between 8 and 16: 16 for FP8 / INT8 at K = 8192,
@@ -534,13 +582,14 @@ static int launch(const void* A, const void* B, void* D, int M, int N, int K, cu
 // Arguments shared by the four entry points. Operand pitches must be
 // multiples of 16 bytes for TMA: M and K multiples of 16 / element size.
 template <class C>
-static int checked_launch(const void* A, const void* B, void* D, int M, int N, int K, cudaStream_t stream) {
+static int checked_launch(const void* A, const void* B, void* D, int M, int N, int K, cudaStream_t stream,
+                          bool accumulate = false) {
     if (M < 0 || N < 0 || K < 0) return GPLK_STATUS_BAD_ARG;
     if (M == 0 || N == 0) return GPLK_STATUS_OK;
     constexpr int align = 16 / C::kInBytes;
     if (K == 0 || M % align != 0 || K % align != 0) return GPLK_STATUS_BAD_ARG;
     if (!A || !B || !D || !aligned16(A) || !aligned16(B)) return GPLK_STATUS_BAD_ARG;
-    return launch<C>(A, B, D, M, N, K, stream);
+    return launch<C>(A, B, D, M, N, K, stream, nullptr, nullptr, accumulate);
 }
 
 }  // namespace pair
@@ -564,4 +613,24 @@ extern "C" int gplk_gemm_tf32_nn(const float* A, const float* B, float* D, int M
 extern "C" int gplk_gemm_i8_nn(const int8_t* A, const int8_t* B, int32_t* D, int M, int N, int K,
                                cudaStream_t stream) {
     return gplk::pair::checked_launch<gplk::pair::CfgI8>(A, B, D, M, N, K, stream);
+}
+
+extern "C" int gplk_gemm_bf16_nn_acc(const uint16_t* A, const uint16_t* B, uint16_t* C, int M, int N, int K,
+                                     cudaStream_t stream) {
+    return gplk::pair::checked_launch<gplk::pair::CfgBF16>(A, B, C, M, N, K, stream, true);
+}
+
+extern "C" int gplk_gemm_f16_nn_acc(const uint16_t* A, const uint16_t* B, uint16_t* C, int M, int N, int K,
+                                    cudaStream_t stream) {
+    return gplk::pair::checked_launch<gplk::pair::CfgF16>(A, B, C, M, N, K, stream, true);
+}
+
+extern "C" int gplk_gemm_tf32_nn_acc(const float* A, const float* B, float* C, int M, int N, int K,
+                                     cudaStream_t stream) {
+    return gplk::pair::checked_launch<gplk::pair::CfgTF32>(A, B, C, M, N, K, stream, true);
+}
+
+extern "C" int gplk_gemm_i8_nn_acc(const int8_t* A, const int8_t* B, int32_t* C, int M, int N, int K,
+                                   cudaStream_t stream) {
+    return gplk::pair::checked_launch<gplk::pair::CfgI8>(A, B, C, M, N, K, stream, true);
 }

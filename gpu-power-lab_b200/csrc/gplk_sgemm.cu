@@ -17,7 +17,6 @@
 // add a few such chains in a fixed order), so the result differs from a
 // double-accumulated host loop only by FP32 rounding.
 #include <mutex>
-#include <thread>
 #include <vector>
 
 #include "gplk_ptx.cuh"
@@ -41,6 +40,26 @@ __device__ __forceinline__ void lds_vec(const float* p, float* out) {
     } else {
 #pragma unroll
         for (int i = 0; i < W; ++i) out[i] = p[i];
+    }
+}
+
+// C = acc + beta * C_old for the W values at p (beta != 0: the old values
+// are read first; fmaf(beta, old, acc) is acc + old exactly rounded once for
+// beta = 1, as cuBLAS computes alpha * acc + beta * C with alpha = 1).
+template <int W>
+__device__ __forceinline__ void add_old_vec(const float* p, float beta, float* v) {
+    if constexpr (W % 4 == 0) {
+#pragma unroll
+        for (int j = 0; j < W; j += 4) {
+            const float4 o = __ldcs(reinterpret_cast<const float4*>(p + j));
+            v[j] = __fmaf_rn(beta, o.x, v[j]);
+            v[j + 1] = __fmaf_rn(beta, o.y, v[j + 1]);
+            v[j + 2] = __fmaf_rn(beta, o.z, v[j + 2]);
+            v[j + 3] = __fmaf_rn(beta, o.w, v[j + 3]);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < W; ++j) v[j] = __fmaf_rn(beta, p[j], v[j]);
     }
 }
 
@@ -102,7 +121,7 @@ struct Cfg {
 template <int BM, int BN, int BK, int TM, int TN, bool VEC>
 __global__ void __launch_bounds__(Cfg<BM, BN, BK, TM, TN, VEC>::kThreads)
     sgemm_kernel(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C,
-                 int M, int N, int K, int lda, int ldb, int ldc) {
+                 int M, int N, int K, int lda, int ldb, int ldc, float beta) {
     using CF = Cfg<BM, BN, BK, TM, TN, VEC>;
     constexpr int T = CF::kThreads;
     constexpr int TM2 = TM / 2, TN2 = TN / 2;
@@ -214,13 +233,14 @@ __global__ void __launch_bounds__(Cfg<BM, BN, BK, TM, TN, VEC>::kThreads)
             for (int g = 0; g < 2; ++g) {
                 const int gn = n0 + g * (BN / 2) + tx * TN2;
                 float* crow = C + (size_t)gm * ldc + gn;
-                const float* v = &acc[h * TM2 + i][g * TN2];
+                float* v = &acc[h * TM2 + i][g * TN2];
                 if (VEC && gn + TN2 <= N) {
+                    if (beta != 0.f) add_old_vec<TN2>(crow, beta, v);
                     stg_vec<TN2>(crow, v);
                 } else {
 #pragma unroll
                     for (int j = 0; j < TN2; ++j)
-                        if (gn + j < N) crow[j] = v[j];
+                        if (gn + j < N) crow[j] = beta != 0.f ? __fmaf_rn(beta, crow[j], v[j]) : v[j];
                 }
             }
         }
@@ -239,7 +259,7 @@ constexpr int kSplitThreads = 256;  // 128 x 128 tile, 8 x 8 per thread
 template <bool VEC>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kSplitThreads)
     sgemm_split2_kernel(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C, int M,
-                        int N, int K, int lda, int ldb, int ldc) {
+                        int N, int K, int lda, int ldb, int ldc, float beta) {
     constexpr int BM = 128, BN = 128, BK = 16, TM = 8, TN = 8;
     using CF = Cfg<BM, BN, BK, TM, TN, VEC>;
     constexpr int T = CF::kThreads;
@@ -377,13 +397,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kSplitThreads)
             for (int g = 0; g < 2; ++g) {
                 const int gn = n0 + g * (BN / 2) + tx * TN2;
                 float* crow = C + (size_t)gm * ldc + gn;
-                const float* val = &acc[h * TM2 + i][g * TN2];
+                float* val = &acc[h * TM2 + i][g * TN2];
                 if (VEC && gn + TN2 <= N) {
+                    if (beta != 0.f) add_old_vec<TN2>(crow, beta, val);
                     stg_vec<TN2>(crow, val);
                 } else {
 #pragma unroll
                     for (int j = 0; j < TN2; ++j)
-                        if (gn + j < N) crow[j] = val[j];
+                        if (gn + j < N) crow[j] = beta != 0.f ? __fmaf_rn(beta, crow[j], val[j]) : val[j];
                 }
             }
         }
@@ -391,7 +412,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kSplitThreads)
 }
 
 static int launch_split2(const float* A, const float* B, float* C, int M, int N, int K, int lda, int ldb, int ldc,
-                         bool vec, cudaStream_t stream) {
+                         float beta, bool vec, cudaStream_t stream) {
     constexpr int BM = 128, BN = 128, BK = 16;
     const int smem = (int)(sizeof(float) * (2 * BK * (BM + 4) + 2 * BK * BN) + 16 * kSplitThreads * sizeof(float4));
     static thread_local uint64_t configured = 0;
@@ -407,9 +428,9 @@ static int launch_split2(const float* A, const float* B, float* C, int M, int N,
     }
     dim3 grid(2 * ((N + BN - 1) / BN), (M + BM - 1) / BM);
     if (vec)
-        sgemm_split2_kernel<true><<<grid, kSplitThreads, smem, stream>>>(A, B, C, M, N, K, lda, ldb, ldc);
+        sgemm_split2_kernel<true><<<grid, kSplitThreads, smem, stream>>>(A, B, C, M, N, K, lda, ldb, ldc, beta);
     else
-        sgemm_split2_kernel<false><<<grid, kSplitThreads, smem, stream>>>(A, B, C, M, N, K, lda, ldb, ldc);
+        sgemm_split2_kernel<false><<<grid, kSplitThreads, smem, stream>>>(A, B, C, M, N, K, lda, ldb, ldc, beta);
     return launch_status(cudaGetLastError());
 }
 
@@ -555,7 +576,7 @@ __device__ __forceinline__ void v2_mainloop(const float* __restrict__ A, const f
 // 4 tx) with bounds checks.
 template <int TN>
 __device__ __forceinline__ void v2_store(float* __restrict__ C, int M, int N, int ldc, int m0, int n0,
-                                         const float2 (&acc)[8][TN / 2]) {
+                                         const float2 (&acc)[8][TN / 2], float beta) {
     using T = V2T<TN>;
     const int tid = threadIdx.x;
     const int tx = tid % T::TX, ty = tid / T::TX;
@@ -567,13 +588,14 @@ __device__ __forceinline__ void v2_store(float* __restrict__ C, int M, int N, in
         for (int h = 0; h < T::NG; ++h) {
             const int gn = n0 + h * T::GS + tx * 4;
             float* crow = C + (size_t)gm * ldc + gn;
-            const float v[4] = {acc[i][2 * h].x, acc[i][2 * h].y, acc[i][2 * h + 1].x, acc[i][2 * h + 1].y};
+            float v[4] = {acc[i][2 * h].x, acc[i][2 * h].y, acc[i][2 * h + 1].x, acc[i][2 * h + 1].y};
             if (gn + 4 <= N) {
+                if (beta != 0.f) add_old_vec<4>(crow, beta, v);
                 stg_vec<4>(crow, v);
             } else {
 #pragma unroll
                 for (int j = 0; j < 4; ++j)
-                    if (gn + j < N) crow[j] = v[j];
+                    if (gn + j < N) crow[j] = beta != 0.f ? __fmaf_rn(beta, crow[j], v[j]) : v[j];
             }
         }
     }
@@ -582,7 +604,7 @@ __device__ __forceinline__ void v2_store(float* __restrict__ C, int M, int N, in
 template <int TN>
 __global__ void __launch_bounds__(V2T<TN>::Threads, 1)
     sgemm_v2_kernel(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C, int M, int N,
-                    int K, int lda, int ldb, int ldc) {
+                    int K, int lda, int ldb, int ldc, float beta) {
     using T = V2T<TN>;
     extern __shared__ __align__(16) float v2_smem[];
     const int m0 = blockIdx.y * kV2BM, n0 = blockIdx.x * kV2BN;
@@ -592,7 +614,7 @@ __global__ void __launch_bounds__(V2T<TN>::Threads, 1)
 #pragma unroll
         for (int j = 0; j < T::NP; ++j) acc[i][j] = make_float2(0.f, 0.f);
     v2_mainloop<TN>(A, B, M, N, lda, ldb, m0, n0, 0, K, v2_smem, acc);
-    v2_store<TN>(C, M, N, ldc, m0, n0, acc);
+    v2_store<TN>(C, M, N, ldc, m0, n0, acc, beta);
 }
 
 // ------------------------------------------------------------ stream-K
@@ -623,8 +645,8 @@ __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
 constexpr int kSkThreads = V2T<kV2TNStreamK>::Threads;
 __global__ void __launch_bounds__(kSkThreads, 1)
     sgemm_sk_kernel(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C, int M, int N,
-                    int K, int lda, int ldb, int ldc, float4* __restrict__ ws, unsigned* __restrict__ flags,
-                    unsigned epoch) {
+                    int K, int lda, int ldb, int ldc, float beta, float4* __restrict__ ws,
+                    unsigned* __restrict__ flags, unsigned epoch) {
     constexpr int TN = kV2TNStreamK;
     using T = V2T<TN>;
     extern __shared__ __align__(16) float v2_smem[];
@@ -702,14 +724,14 @@ __global__ void __launch_bounds__(kSkThreads, 1)
                     if (qe >= tile_u1) break;
                 }
             }
-            v2_store<TN>(C, M, N, ldc, m0, n0, acc);
+            v2_store<TN>(C, M, N, ldc, m0, n0, acc, beta);
         }
         u = tile_u0 + ke;
     }
 }
 
 static int launch_v2(const float* A, const float* B, float* C, int M, int N, int K, int lda, int ldb, int ldc,
-                     cudaStream_t stream) {
+                     float beta, cudaStream_t stream) {
     constexpr int TN = kV2TNDense;
     const int smem = (int)(sizeof(float) * kV2Stages * (kV2AStage + kV2BStage));
     static thread_local uint64_t configured = 0;
@@ -722,30 +744,34 @@ static int launch_v2(const float* A, const float* B, float* C, int M, int N, int
         configured |= 1ull << dev;
     }
     const int nt = (N + kV2BN - 1) / kV2BN, mt = (M + kV2BM - 1) / kV2BM;
-    sgemm_v2_kernel<TN><<<dim3(nt, mt), V2T<TN>::Threads, smem, stream>>>(A, B, C, M, N, K, lda, ldb, ldc);
+    sgemm_v2_kernel<TN><<<dim3(nt, mt), V2T<TN>::Threads, smem, stream>>>(A, B, C, M, N, K, lda, ldb, ldc, beta);
     return launch_status(cudaGetLastError());
 }
 
-// One stream-K workspace per (device, stream): partial-tile slots and flags
-// for one CTA per SM. Concurrent GEMMs on different streams never share one
-// (cudaStreamPerThread is a different stream in each host thread, so it is
-// keyed by thread too); GEMMs on one stream are ordered by the stream. Allocated on first use
-// (cudaMalloc, so the first call for a stream must not be inside a CUDA
-// graph capture) and kept for the life of the process.
-struct SkSlot {
+// The stream-K workspace is the caller's: a flag per CTA (the first 256
+// bytes hold up to 64 flags, more take further 256-byte blocks) followed by
+// one parked partial tile per CTA (64 KiB). A flag holds the launch's epoch.
+// The epochs live on the host, per (device, workspace address): the first
+// launch that sees a workspace zeroes its flags on the stream (an
+// asynchronous memset, no allocation); every launch then takes the next
+// epoch, so a flag left raised by a launch that timed out never reads as
+// fresh to a later one.
+constexpr size_t kSkPartBytes = (size_t)V2T<kV2TNStreamK>::Park * kSkThreads * sizeof(float4);
+
+static size_t sk_flag_bytes(int ctas) { return (((size_t)ctas * sizeof(unsigned)) + 255) & ~(size_t)255; }
+static size_t sk_workspace_bytes(int ctas) { return sk_flag_bytes(ctas) + (size_t)ctas * kSkPartBytes; }
+
+struct SkEpoch {
     int device;
-    cudaStream_t stream;
-    std::thread::id thread;  // set only for cudaStreamPerThread, whose handle names one stream per thread
+    const void* ws;
     int ctas;
-    float4* ws;
-    unsigned* flags;
     unsigned epoch;
 };
 static std::mutex g_sk_mu;
-static std::vector<SkSlot> g_sk_slots;
+static std::vector<SkEpoch> g_sk_epochs;
 
 static int launch_sk(const float* A, const float* B, float* C, int M, int N, int K, int lda, int ldb, int ldc,
-                     int sm_count, cudaStream_t stream) {
+                     float beta, int sm_count, void* workspace, cudaStream_t stream) {
     const int smem = (int)(sizeof(float) * kV2Stages * (kV2AStage + kV2BStage));
     int dev = 0;
     cudaGetDevice(&dev);
@@ -762,38 +788,24 @@ static int launch_sk(const float* A, const float* B, float* C, int M, int N, int
         per_sm < 1)
         return GPLK_STATUS_UNSUPPORTED;
     const int G = sm_count;
-    float4* ws = nullptr;
-    unsigned* flags = nullptr;
+    unsigned* flags = static_cast<unsigned*>(workspace);
+    float4* ws = reinterpret_cast<float4*>(static_cast<uint8_t*>(workspace) + sk_flag_bytes(G));
     unsigned epoch = 0;
     {
         std::lock_guard<std::mutex> lock(g_sk_mu);
-        const std::thread::id thread =
-            stream == cudaStreamPerThread ? std::this_thread::get_id() : std::thread::id();
-        SkSlot* slot = nullptr;
-        for (SkSlot& s : g_sk_slots)
-            if (s.device == dev && s.stream == stream && s.thread == thread && s.ctas == G) slot = &s;
-        if (!slot) {
-            SkSlot s{dev, stream, thread, G, nullptr, nullptr, 0u};
-            if (cudaMalloc(&s.ws, (size_t)G * V2T<kV2TNStreamK>::Park * kSkThreads * sizeof(float4)) != cudaSuccess)
-                return GPLK_STATUS_CUDA_ERROR;
-            if (cudaMalloc(&s.flags, (size_t)G * sizeof(unsigned)) != cudaSuccess) {
-                cudaFree(s.ws);
-                return GPLK_STATUS_CUDA_ERROR;
-            }
-            if (cudaMemsetAsync(s.flags, 0, (size_t)G * sizeof(unsigned), stream) != cudaSuccess) {
-                cudaFree(s.ws);
-                cudaFree(s.flags);
-                return GPLK_STATUS_LAUNCH_FAIL;
-            }
-            g_sk_slots.push_back(s);
-            slot = &g_sk_slots.back();
+        SkEpoch* e = nullptr;
+        for (SkEpoch& x : g_sk_epochs)
+            if (x.device == dev && x.ws == workspace && x.ctas == G) e = &x;
+        if (!e) {
+            if (g_sk_epochs.size() >= 256) g_sk_epochs.clear();  // forgotten workspaces are zeroed again
+            if (cudaMemsetAsync(flags, 0, sk_flag_bytes(G), stream) != cudaSuccess) return GPLK_STATUS_LAUNCH_FAIL;
+            g_sk_epochs.push_back(SkEpoch{dev, workspace, G, 0u});
+            e = &g_sk_epochs.back();
         }
-        if (++slot->epoch == 0u) slot->epoch = 1u;
-        ws = slot->ws;
-        flags = slot->flags;
-        epoch = slot->epoch;
+        if (++e->epoch == 0u) e->epoch = 1u;
+        epoch = e->epoch;
     }
-    void* args[] = {&A, &B, &C, &M, &N, &K, &lda, &ldb, &ldc, &ws, &flags, &epoch};
+    void* args[] = {&A, &B, &C, &M, &N, &K, &lda, &ldb, &ldc, &beta, &ws, &flags, &epoch};
     if (cudaLaunchCooperativeKernel((const void*)sgemm_sk_kernel, dim3((unsigned)G), dim3(kSkThreads), args,
                                     (size_t)smem, stream) != cudaSuccess)
         return GPLK_STATUS_LAUNCH_FAIL;
@@ -802,50 +814,78 @@ static int launch_sk(const float* A, const float* B, float* C, int M, int N, int
 
 template <int BM, int BN, int BK, int TM, int TN>
 static int launch(const float* A, const float* B, float* C, int M, int N, int K, int lda, int ldb,
-                  int ldc, bool vec, cudaStream_t stream) {
+                  int ldc, float beta, bool vec, cudaStream_t stream) {
     dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
     if (vec) {
-        sgemm_kernel<BM, BN, BK, TM, TN, true>
-            <<<grid, Cfg<BM, BN, BK, TM, TN, true>::kThreads, 0, stream>>>(A, B, C, M, N, K, lda, ldb, ldc);
+        sgemm_kernel<BM, BN, BK, TM, TN, true><<<grid, Cfg<BM, BN, BK, TM, TN, true>::kThreads, 0, stream>>>(
+            A, B, C, M, N, K, lda, ldb, ldc, beta);
     } else {
-        sgemm_kernel<BM, BN, BK, TM, TN, false>
-            <<<grid, Cfg<BM, BN, BK, TM, TN, false>::kThreads, 0, stream>>>(A, B, C, M, N, K, lda, ldb, ldc);
+        sgemm_kernel<BM, BN, BK, TM, TN, false><<<grid, Cfg<BM, BN, BK, TM, TN, false>::kThreads, 0, stream>>>(
+            A, B, C, M, N, K, lda, ldb, ldc, beta);
     }
     return launch_status(cudaGetLastError());
+}
+
+// Which kernel a problem takes (the 16-byte-aligned case decides the
+// workspace size: only stream-K needs one).
+enum class Plan { StreamK, V2, Tiles128, Split2, Tiles64 };
+
+static Plan plan(int M, int N, int K, bool vec, int sm_count) {
+    // 128 x 128 tiles. When they leave more than a tenth of the last wave's
+    // SMs idle, stream-K spreads the K steps evenly over one CTA per SM;
+    // tiny or shallow problems fall back to 64 x 64 tiles.
+    const long tiles128 = (long)((M + 127) / 128) * ((N + 127) / 128);
+    if (vec) {
+        const long waves = (tiles128 + sm_count - 1) / sm_count;
+        const bool ragged = tiles128 * 10 < waves * sm_count * 9;
+        if (K >= 256 && 4 * tiles128 >= sm_count && ragged) return Plan::StreamK;
+        if (tiles128 * 2 >= sm_count / 4) return Plan::V2;
+    }
+    if (tiles128 >= sm_count) return Plan::Tiles128;
+    if (K >= 256 && 2 * tiles128 >= sm_count / 2) return Plan::Split2;
+    return Plan::Tiles64;
 }
 
 }  // namespace sgemm
 }  // namespace gplk
 
-extern "C" int gplk_sgemm_f32(const float* A, const float* B, float* C, int M, int N, int K, int lda,
-                              int ldb, int ldc, cudaStream_t stream) {
+extern "C" size_t gplk_sgemm_workspace_bytes(int M, int N, int K) {
+    using namespace gplk;
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    DeviceInfo d;
+    if (current_device_info(&d) != GPLK_STATUS_OK) return 0;
+    return sgemm::plan(M, N, K, true, d.sm_count) == sgemm::Plan::StreamK ? sgemm::sk_workspace_bytes(d.sm_count)
+                                                                          : 0;
+}
+
+extern "C" int gplk_sgemm_f32(const float* A, const float* B, float* C, int M, int N, int K, int lda, int ldb,
+                              int ldc, float beta, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
     using namespace gplk;
     if (M < 0 || N < 0 || K < 0) return GPLK_STATUS_BAD_ARG;
     if (M == 0 || N == 0) return GPLK_STATUS_OK;
     if (!C || (K > 0 && (!A || !B))) return GPLK_STATUS_BAD_ARG;  // K == 0: A, B unread
     if ((K > 0 && (lda < K || ldb < N)) || ldc < N) return GPLK_STATUS_BAD_ARG;
+    if (workspace && !aligned16(workspace)) return GPLK_STATUS_BAD_ARG;
     DeviceInfo d;
     int st = current_device_info(&d);
     if (st != GPLK_STATUS_OK) return st;
     const bool vec = aligned16(A) && aligned16(B) && aligned16(C) && (lda % 4 == 0) && (ldb % 4 == 0) &&
                      (ldc % 4 == 0) && (K % 4 == 0) && (N % 4 == 0);
-    // 128 x 128 tiles (8 x 8 per thread). When they leave more than a tenth
-    // of the last wave's SMs idle, stream-K spreads the K steps evenly over
-    // one CTA per SM; tiny or shallow problems fall back to 64 x 64 tiles.
-    const long tiles128 = (long)((M + 127) / 128) * ((N + 127) / 128);
-    if (vec) {  // 16-byte aligned rows: the cp.async + FFMA2 kernels
-        const long waves = (tiles128 + d.sm_count - 1) / d.sm_count;
-        const bool ragged = tiles128 * 10 < waves * d.sm_count * 9;
-        if (K >= 256 && 4 * tiles128 >= d.sm_count && ragged) {
-            const int st = sgemm::launch_sk(A, B, C, M, N, K, lda, ldb, ldc, d.sm_count, stream);
-            if (st != GPLK_STATUS_UNSUPPORTED) return st;
-        }
-        if (tiles128 * 2 >= d.sm_count / 4)
-            return sgemm::launch_v2(A, B, C, M, N, K, lda, ldb, ldc, stream);
+    switch (sgemm::plan(M, N, K, vec, d.sm_count)) {
+        case sgemm::Plan::StreamK:
+            if (workspace && workspace_bytes >= sgemm::sk_workspace_bytes(d.sm_count)) {
+                st = sgemm::launch_sk(A, B, C, M, N, K, lda, ldb, ldc, beta, d.sm_count, workspace, stream);
+                if (st != GPLK_STATUS_UNSUPPORTED) return st;
+            }
+            // No (or too small a) workspace: the whole-tile kernel instead.
+            return sgemm::launch_v2(A, B, C, M, N, K, lda, ldb, ldc, beta, stream);
+        case sgemm::Plan::V2:
+            return sgemm::launch_v2(A, B, C, M, N, K, lda, ldb, ldc, beta, stream);
+        case sgemm::Plan::Tiles128:
+            return sgemm::launch<128, 128, 16, 8, 8>(A, B, C, M, N, K, lda, ldb, ldc, beta, vec, stream);
+        case sgemm::Plan::Split2:
+            return sgemm::launch_split2(A, B, C, M, N, K, lda, ldb, ldc, beta, vec, stream);
+        default:
+            return sgemm::launch<64, 64, 16, 4, 4>(A, B, C, M, N, K, lda, ldb, ldc, beta, vec, stream);
     }
-    if (tiles128 >= d.sm_count)
-        return sgemm::launch<128, 128, 16, 8, 8>(A, B, C, M, N, K, lda, ldb, ldc, vec, stream);
-    if (K >= 256 && 2 * tiles128 >= d.sm_count / 2)
-        return sgemm::launch_split2(A, B, C, M, N, K, lda, ldb, ldc, vec, stream);
-    return sgemm::launch<64, 64, 16, 4, 4>(A, B, C, M, N, K, lda, ldb, ldc, vec, stream);
 }

@@ -83,14 +83,17 @@ def lib() -> ctypes.CDLL:
     L.gplk_copy_f32.restype = _i
     L.gplk_copy_f32.argtypes = [_p, _p, _sz, _p]
     L.gplk_sgemm_f32.restype = _i
-    L.gplk_sgemm_f32.argtypes = [_p, _p, _p, _i, _i, _i, _i, _i, _i, _p]
+    L.gplk_sgemm_f32.argtypes = [_p, _p, _p, _i, _i, _i, _i, _i, _i, _f, _p, _sz, _p]
+    L.gplk_sgemm_workspace_bytes.restype = _sz
+    L.gplk_sgemm_workspace_bytes.argtypes = [_i, _i, _i]
     L.gplk_gemm_fp8_tn.restype = _i
     L.gplk_gemm_fp8_tn.argtypes = [_p, _p, _p, _i, _i, _i, _p, _p, _p]
     L.gplk_gemm_nvfp4_tn.restype = _i
     L.gplk_gemm_nvfp4_tn.argtypes = [_p, _p, _p, _p, _p, _i, _i, _i, _p, _p]
     for name in ("gplk_gemm_bf16_nn", "gplk_gemm_f16_nn", "gplk_gemm_tf32_nn", "gplk_gemm_i8_nn"):
-        getattr(L, name).restype = _i
-        getattr(L, name).argtypes = [_p, _p, _p, _i, _i, _i, _p]
+        for nm in (name, name + "_acc"):
+            getattr(L, nm).restype = _i
+            getattr(L, nm).argtypes = [_p, _p, _p, _i, _i, _i, _p]
     L.gplk_selftest_wait_timeout.restype = _i
     L.gplk_selftest_wait_timeout.argtypes = [ctypes.c_ulonglong, _p, _p]
     L.gplk_nvfp4_sf_bytes.restype = _sz
@@ -153,13 +156,44 @@ def copy(dst, src, stream=None) -> None:
 
 # ------------------------------------------------------------ SGEMM
 
-def sgemm(A, B, C, stream=None) -> None:
-    """Row-major C = A @ B in FP32 (A: M x K, B: K x N, C: M x N)."""
+def sgemm_workspace_bytes(M: int, N: int, K: int) -> int:
+    """Bytes of stream-K workspace gplk_sgemm_f32 uses for this shape on the
+    current device (0: the shape runs on whole tiles)."""
+    return int(lib().gplk_sgemm_workspace_bytes(M, N, K))
+
+
+_sgemm_ws: dict = {}
+
+
+def _workspace(nbytes: int, stream):
+    """A workspace of at least nbytes for `stream`, kept per (device, stream)
+    so GEMMs on one stream share it and GEMMs on different streams never do.
+    torch allocates it (the library itself allocates nothing)."""
+    import torch
+
+    s = stream if stream is not None else torch.cuda.current_stream()
+    key = (s.device.index if s.device.index is not None else torch.cuda.current_device(), s.cuda_stream)
+    ws = _sgemm_ws.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=s.device)
+        _sgemm_ws[key] = ws
+    return ws
+
+
+def sgemm(A, B, C, stream=None, beta: float = 0.0, workspace="auto") -> None:
+    """Row-major C = A @ B + beta * C in FP32 (A: M x K, B: K x N, C: M x N).
+    workspace: "auto" (a cached per-stream buffer), None (no stream-K), or a
+    uint8 CUDA tensor."""
     M, K = A.shape
     K2, N = B.shape
     assert K == K2 and tuple(C.shape) == (M, N)
-    _check("gplk_sgemm_f32", lib().gplk_sgemm_f32(_ptr(A), _ptr(B), _ptr(C), M, N, K, A.stride(0),
-                                                    B.stride(0), C.stride(0), _stream(stream)))
+    if isinstance(workspace, str):
+        need = sgemm_workspace_bytes(M, N, K)
+        workspace = _workspace(need, stream) if need else None
+    wp = workspace.data_ptr() if workspace is not None else None
+    wb = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    _check("gplk_sgemm_f32", lib().gplk_sgemm_f32(_ptr(A), _ptr(B), _ptr(C), M, N, K, A.stride(0), B.stride(0),
+                                                    C.stride(0), float(beta), wp, wb, _stream(stream)))
 
 
 # ------------------------------------------------------------ narrow GEMMs
@@ -193,13 +227,14 @@ def gemm_nvfp4_tn(A, B, SFA, SFB, D, K: int, alpha, stream=None) -> None:
 _NN = {"bf16": "gplk_gemm_bf16_nn", "f16": "gplk_gemm_f16_nn", "tf32": "gplk_gemm_tf32_nn", "i8": "gplk_gemm_i8_nn"}
 
 
-def gemm_nn(prec: str, A, B, D, M: int, N: int, K: int, stream=None) -> None:
-    """Column-major D = A @ B (cublasGemmEx NN layout). A holds M x K with
-    M contiguous, B holds K x N with K contiguous, D holds M x N with M
-    contiguous: as torch tensors, A is (K, M), B is (N, K) and D is (N, M),
-    all contiguous. prec: bf16 | f16 | tf32 | i8."""
+def gemm_nn(prec: str, A, B, D, M: int, N: int, K: int, stream=None, accumulate: bool = False) -> None:
+    """Column-major D = A @ B (cublasGemmEx NN layout), or D = A @ B + D with
+    accumulate (beta = 1). A holds M x K with M contiguous, B holds K x N
+    with K contiguous, D holds M x N with M contiguous: as torch tensors, A
+    is (K, M), B is (N, K) and D is (N, M), all contiguous.
+    prec: bf16 | f16 | tf32 | i8."""
     assert A.numel() == M * K and B.numel() == K * N and D.numel() == M * N
-    fn = _NN[prec]
+    fn = _NN[prec] + ("_acc" if accumulate else "")
     _check(fn, getattr(lib(), fn)(_ptr(A), _ptr(B), _ptr(D), M, N, K, _stream(stream)))
 
 

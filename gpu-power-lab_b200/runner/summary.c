@@ -23,6 +23,11 @@
  *      document, which gpu-power-lab_b200/runner/rung-summary.schema.v1x.json
  *      describes.
  *
+ * The extended document's `transient` block also carries `fabric` (the
+ * per-cycle allreduce of the multi-GPU powervirus rung: implementation,
+ * rank, world, bytes, cycles, median and max time, bus bandwidth) when that
+ * step ran; the reference has no such step.
+ *
  * Strings are JSON-escaped and non-finite numbers are written as 0, so the
  * output always parses (an error message with a quote in it does not break
  * the document).
@@ -35,7 +40,13 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include "fabric_step.h"
 #include "util.h"
+
+/* The multi-GPU powervirus rung's per-cycle fabric step reports through
+ * gpl_fabric_stats (fabric_step.cu). A weak reference: an emitter linked
+ * without that file sees NULL and writes no fabric block. */
+#pragma weak gpl_fabric_stats
 
 /* ---- device identity ---------------------------------------------------- */
 
@@ -340,6 +351,19 @@ int gpl_summary_emit(FILE *out, const gpl_args_t *args, const gpl_device_info_t 
         jw_num(&w, "energy_gap_pct", "%.3f", gap_pct);
         jw_int(&w, "sample_hz_requested", args->sample_hz);
         jw_num(&w, "sample_hz_achieved", "%.1f", achieved_hz);
+        const gpl_fabric_stats_t *fs = gpl_fabric_stats ? gpl_fabric_stats() : NULL;
+        if (fs && fs->active) {
+            jw_open(&w, "fabric", '{');
+            jw_str(&w, "impl", fs->impl);
+            jw_int(&w, "rank", fs->rank);
+            jw_int(&w, "world", fs->world);
+            jw_u64(&w, "bytes", (unsigned long long)fs->bytes);
+            jw_u64(&w, "cycles", fs->cycles);
+            jw_num(&w, "median_ms", "%.4f", fs->median_ms);
+            jw_num(&w, "max_ms", "%.4f", fs->max_ms);
+            jw_num(&w, "busbw_gbs", "%.2f", fs->busbw_gbs);
+            jw_close(&w, '}');
+        }
         jw_close(&w, '}');
     }
 

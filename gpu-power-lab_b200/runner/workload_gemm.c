@@ -10,10 +10,13 @@
  *   bf16, fp16, tf32, int8
  *                gplk_gemm_{bf16,f16,tf32,i8}_nn: tcgen05 GEMMs on CTA pairs in
  *                the same column-major NN layout and output types as the
- *                reference's cublasGemmEx call (:45-79, :155-163).
- *                GPL_GEMM_BACKEND=cublas keeps these on cublasGemmEx.
+ *                reference's cublasGemmEx call (:45-79, :155-163)
  *   fp64         cublasGemmEx with the reference's type mapping: a plain
- *                library GEMM (tcgen05 has no FP64 kind)
+ *                library GEMM, the one precision left on it (tcgen05 has no
+ *                FP64 kind)
+ * The fp32 SGEMM's stream-K workspace (gplk_sgemm_workspace_bytes) is
+ * allocated once per stream at set-up, beside the operands; the GEMM calls
+ * in the timed loops allocate nothing.
  *
  * Square N x N x N problems, one C per stream, warm-up and steady phases by
  * wall clock, a device sync every 8 x streams launches (:167-219).
@@ -44,14 +47,11 @@ static gemm_path_t path_for(gpl_prec_t p) {
     if (p == GPL_PREC_FP32) return PATH_GPLK_SGEMM;
     if (p == GPL_PREC_FP8 || p == GPL_PREC_FP4) return PATH_GPLK_LT;
     if (p == GPL_PREC_FP64) return PATH_CUBLAS;
-    const char *b = getenv("GPL_GEMM_BACKEND");
-    if (b && !strcmp(b, "cublas")) return PATH_CUBLAS;
     return PATH_GPLK_TC;
 }
 
-#define TC_SIZE_MSG                                                                      \
-    "size unsupported by the tcgen05 GEMM (a multiple of 8 for bf16/fp16, 4 for tf32, 16 " \
-    "for int8 is required); GPL_GEMM_BACKEND=cublas runs it on cublasGemmEx"
+#define TC_SIZE_MSG \
+    "size unsupported by the tcgen05 GEMM (a multiple of 8 for bf16/fp16, 4 for tf32, 16 for int8 is required)"
 
 /* One tcgen05 GEMM of the rung's precision: column-major C = A * B. */
 static int gplk_tc_gemm(gpl_prec_t p, const void *A, const void *B, void *C, int n, cudaStream_t s) {
@@ -115,10 +115,12 @@ int gpl_workload_gemm_run(gpl_workload_ctx_t *ctx) {
     bool aborted = false;
     void *dA = NULL, *dB = NULL;
     void **dC = (void **)calloc((size_t)ns, sizeof(void *));
+    void **dW = (void **)calloc((size_t)ns, sizeof(void *)); /* SGEMM stream-K workspace per stream */
+    size_t ws_bytes = 0;
     cudaStream_t *st = (cudaStream_t *)calloc((size_t)ns, sizeof(cudaStream_t));
     gemm_cublas_t *cb = (gemm_cublas_t *)calloc((size_t)ns, sizeof(gemm_cublas_t));
     gpl_lt_gemm_t *lt = (gpl_lt_gemm_t *)calloc((size_t)ns, sizeof(gpl_lt_gemm_t));
-    if (!dC || !st || !cb || !lt) {
+    if (!dC || !dW || !st || !cb || !lt) {
         ctx->error = "oom (host arrays)";
         rc = -1;
         goto cleanup;
@@ -158,9 +160,11 @@ int gpl_workload_gemm_run(gpl_workload_ctx_t *ctx) {
         G_CUDA(cudaMalloc(&dB, nn * in_b));
         G_CUDA(cudaMemset(dA, 0x3c, nn * in_b));
         G_CUDA(cudaMemset(dB, 0x3c, nn * in_b));
+        if (path == PATH_GPLK_SGEMM) ws_bytes = gplk_sgemm_workspace_bytes(N, N, N);
         for (int i = 0; i < ns; i++) {
             G_CUDA(cudaMalloc(&dC[i], nn * out_b));
             G_CUDA(cudaMemset(dC[i], 0, nn * out_b));
+            if (ws_bytes) G_CUDA(cudaMalloc(&dW[i], ws_bytes));
             if (path == PATH_CUBLAS) {
                 cb[i] = cb[0];
                 if (cublasCreate(&cb[i].h) != CUBLAS_STATUS_SUCCESS ||
@@ -183,7 +187,7 @@ int gpl_workload_gemm_run(gpl_workload_ctx_t *ctx) {
         int _r = 0;                                                                                     \
         if (path == PATH_GPLK_SGEMM) {                                                                  \
             _r = gplk_sgemm_f32((const float *)dB, (const float *)dA, (float *)dC[i], N, N, N, N, N, N, \
-                                st[i]);                                                                 \
+                                0.0f, dW[i], ws_bytes, st[i]);                                          \
             if (_r) ctx->error = gplk_status_string(_r);                                                \
         } else if (path == PATH_GPLK_LT) {                                                              \
             _r = gpl_lt_enqueue(&lt[i], 1);                                                             \
@@ -263,10 +267,12 @@ cleanup:
         if (cb && cb[i].h) cublasDestroy(cb[i].h);
         if (st && st[i]) cudaStreamDestroy(st[i]);
         if (dC && dC[i]) cudaFree(dC[i]);
+        if (dW && dW[i]) cudaFree(dW[i]);
     }
     if (dA) cudaFree(dA);
     if (dB) cudaFree(dB);
     free(dC);
+    free(dW);
     free(st);
     free(cb);
     free(lt);

@@ -9,11 +9,16 @@
  * in-kernel tcgen05 (one thread issues FP8 MMAs into TMEM), replacing the
  * warp-synchronous wmma role. With --tensor-backend cublas the tensor role
  * leaves the kernel, as in the reference, and GEMMs run on a concurrent
- * stream: fp8/fp4 through gpl_lt_* (libgplk tcgen05 GEMMs, now including a
- * working NVFP4), bf16/fp16/tf32/int8 through libgplk's tcgen05 NN GEMMs
- * (D = A * B; GPL_GEMM_BACKEND=cublas keeps the reference's cublasGemmEx
- * with beta = 1), fp32 and fp64 through cublasGemmEx with beta = 1.
- * Ramped duty edges shape the kernel's block count.
+ * stream with the reference's semantics (runner/src/workload_powervirus.cu:
+ * 281-397): fp8/fp4 through gpl_lt_* (libgplk tcgen05 GEMMs, D = A^T B,
+ * now including a working NVFP4); bf16/fp16/tf32/int8 through libgplk's
+ * tcgen05 NN GEMMs with beta = 1 (C = A * B + C, "beta=1 keeps C live");
+ * fp32 through libgplk's SIMT SGEMM with beta = 1 (true FP32: the
+ * reference's cublasGemmEx here ran with CUBLAS_TENSOR_OP_MATH, which lets
+ * cuBLAS round FP32 operands down for the tensor cores); fp64 through
+ * cublasGemmEx with beta = 1, the one precision left on the library
+ * (tcgen05 has no FP64 kind). Ramped duty edges shape the kernel's block
+ * count.
  */
 #include "workload.h"
 
@@ -24,6 +29,7 @@
 #include <string.h>
 #include <time.h>
 
+#include "fabric_step.h"
 #include "gemm_lt.h"
 #include "gpl_fault.h"
 #include "gplk.h"
@@ -34,11 +40,13 @@ namespace {
 struct TensorStream {
     gpl_lt_gemm_t lt;
     bool use_lt = false;
-    bool use_gplk = false;  // tcgen05 NN GEMM of the rung's precision
+    bool use_gplk = false;  // libgplk GEMM of the rung's precision (all but fp64)
     gpl_prec_t prec = GPL_PREC_FP16;
     cublasHandle_t h = nullptr;
     cudaStream_t stream = nullptr;
     void *dA = nullptr, *dB = nullptr, *dC = nullptr;
+    void *dW = nullptr;  // fp32 SGEMM stream-K workspace
+    size_t ws_bytes = 0;
     int n = 0;
     cudaDataType in_t = CUDA_R_16F, out_t = CUDA_R_16F;
     cublasComputeType_t comp_t = CUBLAS_COMPUTE_16F;
@@ -63,12 +71,7 @@ int tensor_stream_init(gpl_workload_ctx_t *ctx, TensorStream *ts) {
     }
     size_t in_b = 2, out_b = 2;
     ts->prec = a->precision;
-    {
-        const char *b = getenv("GPL_GEMM_BACKEND");
-        const bool cublas = b && !strcmp(b, "cublas");
-        ts->use_gplk = !cublas && (a->precision == GPL_PREC_BF16 || a->precision == GPL_PREC_FP16 ||
-                                   a->precision == GPL_PREC_TF32 || a->precision == GPL_PREC_INT8);
-    }
+    ts->use_gplk = a->precision != GPL_PREC_FP64;
     switch (a->precision) {
         case GPL_PREC_FP32: ts->in_t = ts->out_t = CUDA_R_32F; ts->comp_t = CUBLAS_COMPUTE_32F; in_b = out_b = 4; break;
         case GPL_PREC_TF32: ts->in_t = ts->out_t = CUDA_R_32F; ts->comp_t = CUBLAS_COMPUTE_32F_FAST_TF32; in_b = out_b = 4; break;
@@ -86,6 +89,13 @@ int tensor_stream_init(gpl_workload_ctx_t *ctx, TensorStream *ts) {
     cudaMemset(ts->dA, 0x3c, nn * in_b);
     cudaMemset(ts->dB, 0x3c, nn * in_b);
     cudaMemset(ts->dC, 0, nn * out_b);
+    if (ts->prec == GPL_PREC_FP32) {
+        ts->ws_bytes = gplk_sgemm_workspace_bytes(ts->n, ts->n, ts->n);
+        if (ts->ws_bytes && cudaMalloc(&ts->dW, ts->ws_bytes) != cudaSuccess) {
+            ctx->error = "tensor stream: out of memory";
+            return -1;
+        }
+    }
     if (ts->use_gplk) {
         ts->active = true;
         return 0;
@@ -100,7 +110,8 @@ int tensor_stream_init(gpl_workload_ctx_t *ctx, TensorStream *ts) {
     return 0;
 }
 
-// `count` GEMMs on the tensor stream, asynchronous. beta = 1 keeps C live.
+// `count` GEMMs on the tensor stream, asynchronous. beta = 1 keeps C live
+// (C = A * B + C), as in the reference; the Lt formats write D = A^T B.
 int tensor_stream_enqueue(TensorStream *ts, int count) {
     if (!ts->active || count <= 0) return 0;
     if (ts->use_lt) return gpl_lt_enqueue(&ts->lt, count);
@@ -110,20 +121,24 @@ int tensor_stream_enqueue(TensorStream *ts, int count) {
             int st = GPLK_STATUS_BAD_ARG;
             switch (ts->prec) {
                 case GPL_PREC_BF16:
-                    st = gplk_gemm_bf16_nn((const uint16_t *)ts->dA, (const uint16_t *)ts->dB, (uint16_t *)ts->dC, n,
-                                           n, n, ts->stream);
+                    st = gplk_gemm_bf16_nn_acc((const uint16_t *)ts->dA, (const uint16_t *)ts->dB,
+                                               (uint16_t *)ts->dC, n, n, n, ts->stream);
                     break;
                 case GPL_PREC_FP16:
-                    st = gplk_gemm_f16_nn((const uint16_t *)ts->dA, (const uint16_t *)ts->dB, (uint16_t *)ts->dC, n,
-                                          n, n, ts->stream);
+                    st = gplk_gemm_f16_nn_acc((const uint16_t *)ts->dA, (const uint16_t *)ts->dB,
+                                              (uint16_t *)ts->dC, n, n, n, ts->stream);
                     break;
                 case GPL_PREC_TF32:
-                    st = gplk_gemm_tf32_nn((const float *)ts->dA, (const float *)ts->dB, (float *)ts->dC, n, n, n,
-                                           ts->stream);
+                    st = gplk_gemm_tf32_nn_acc((const float *)ts->dA, (const float *)ts->dB, (float *)ts->dC, n, n,
+                                               n, ts->stream);
                     break;
-                default:
-                    st = gplk_gemm_i8_nn((const int8_t *)ts->dA, (const int8_t *)ts->dB, (int32_t *)ts->dC, n, n, n,
-                                         ts->stream);
+                case GPL_PREC_INT8:
+                    st = gplk_gemm_i8_nn_acc((const int8_t *)ts->dA, (const int8_t *)ts->dB, (int32_t *)ts->dC, n,
+                                             n, n, ts->stream);
+                    break;
+                default:  // fp32: column-major C = A * B + C is row-major C^T = B^T A^T + C^T
+                    st = gplk_sgemm_f32((const float *)ts->dB, (const float *)ts->dA, (float *)ts->dC, n, n, n, n,
+                                        n, n, 1.0f, ts->dW, ts->ws_bytes, ts->stream);
                     break;
             }
             if (st != GPLK_STATUS_OK) return -1;
@@ -154,6 +169,7 @@ void tensor_stream_free(TensorStream *ts) {
     if (ts->dA) cudaFree(ts->dA);
     if (ts->dB) cudaFree(ts->dB);
     if (ts->dC) cudaFree(ts->dC);
+    if (ts->dW) cudaFree(ts->dW);
     ts->active = false;
 }
 
@@ -214,6 +230,9 @@ int gpl_workload_powervirus_run(gpl_workload_ctx_t *ctx) {
     unsigned char role_map[GPLK_PV_ROLE_SLOTS];
     gplk_pv_cfg cfg;
     uint64_t t_start, s_start, warmup_ns, steady_ns, burst_ns;
+    bool fabric = false;
+    unsigned long long fabric_cycles = 0, cycles_done = 0;
+    cudaEvent_t join[2] = {nullptr, nullptr};  // the other stream and the tensor stream, joined before the step
     memset(&cfg, 0, sizeof(cfg));
     PV_CHECK(st != NULL, "oom (streams)");
 
@@ -233,6 +252,24 @@ int gpl_workload_powervirus_run(gpl_workload_ctx_t *ctx) {
     if (use_cublas_tensor && tensor_stream_init(ctx, &ts) != 0) {
         rc = -1;
         goto cleanup;
+    }
+    {
+        // The per-cycle fabric step (GPL_FABRIC=gplk|nccl): set up before the
+        // phases start; the rendezvous aligns the ranks.
+        const char *ferr = nullptr;
+        PV_CHECK(gpl_fabric_step_init(&ferr) == 0, ferr);
+        fabric = gpl_fabric_step_enabled() != 0;
+        PV_CHECK(!fabric || duty, "fabric step: it runs once per duty cycle, so --duty-on-ms is required");
+        PV_CHECK(!fabric || !fixed_work, "fabric step: --iters (fixed work) cannot keep the ranks in step");
+        if (fabric) {
+            fabric_cycles = gpl_fabric_cycles(a->steady_sec, a->duty_on_ms, a->duty_off_ms);
+            for (int i = 0; i < (int)(sizeof join / sizeof join[0]); i++) PV_CUDA(cudaEventCreateWithFlags(
+                &join[i], cudaEventDisableTiming));
+            const gpl_fabric_stats_t *fs = gpl_fabric_stats();
+            gpl_logf("  fabric step: %s BF16 allreduce of %.0f MiB, rank %d of %d, after each of %llu cycles%s",
+                     fs->impl, fs->bytes / 1048576.0, fs->rank, fs->world, fabric_cycles,
+                     a->stop_on_throttle ? " (--stop-on-throttle not honoured: the ranks stay in step)" : "");
+        }
     }
 
     w[GPLK_PV_ROLE_TENSOR] = a->tensor_cublas ? 0 : a->mix_tensor;
@@ -255,7 +292,11 @@ int gpl_workload_powervirus_run(gpl_workload_ctx_t *ctx) {
                  gplk_pv_block_threads() / 32, GPLK_PV_ROLE_SLOTS, mix, buf_bytes / 1048576.0);
         if (use_cublas_tensor)
             gpl_logf("  tensor backend: %s GEMM n=%d, %d per batch on a concurrent stream%s",
-                     ts.use_lt ? "tcgen05 (libgplk)" : "cuBLAS", ts.n, gemms_per_batch,
+                     ts.use_lt ? "tcgen05 (libgplk gpl_lt)"
+                     : !ts.use_gplk ? "cuBLAS fp64, beta = 1"
+                     : ts.prec == GPL_PREC_FP32 ? "SIMT FP32 (libgplk), beta = 1"
+                                                : "tcgen05 (libgplk), beta = 1",
+                     ts.n, gemms_per_batch,
                      run_kernel ? "" : " (kernel disabled: tensor-only)");
         else
             gpl_logf("  tensor backend: in-kernel tcgen05 (single-thread issue)");
@@ -306,12 +347,15 @@ int gpl_workload_powervirus_run(gpl_workload_ctx_t *ctx) {
     steady_ns = (uint64_t)(a->steady_sec * 1e9);
     burst_ns = (uint64_t)(a->duty_on_ms * 1e6);
     while (1) {
-        if (fixed_work) {
+        if (fabric) {
+            // A fixed number of cycles on every rank: each ends in a collective.
+            if (cycles_done >= fabric_cycles) break;
+        } else if (fixed_work) {
             if ((long long)ctx->iterations_steady >= a->iters) break;
         } else if (gpl_mono_ns() - s_start >= steady_ns) {
             break;
         }
-        if (a->stop_on_throttle && gpl_telemetry_throttled_now(ctx->tele)) {
+        if (!fabric && a->stop_on_throttle && gpl_telemetry_throttled_now(ctx->tele)) {
             ctx->aborted_on_throttle = true;
             break;
         }
@@ -324,7 +368,9 @@ int gpl_workload_powervirus_run(gpl_workload_ctx_t *ctx) {
                 ramp_ns = (uint64_t)((a->duty_ramp_ms > 0.0 ? a->duty_ramp_ms : a->duty_on_ms * 0.25) * 1e6);
                 if (ramp_ns > burst_ns / 2) ramp_ns = burst_ns / 2;
             }
-            while (gpl_mono_ns() - b0 < burst_ns) {
+            uint64_t launch_ns = 0;  // fabric step: duration of the previous launch
+            while (fabric || gpl_mono_ns() - b0 < burst_ns) {
+                const uint64_t tl = gpl_mono_ns();
                 int nb = sm_count;
                 if (ramp_ns > 0) {
                     const uint64_t el = gpl_mono_ns() - b0;
@@ -342,8 +388,33 @@ int gpl_workload_powervirus_run(gpl_workload_ctx_t *ctx) {
                 PV_TENSOR(gemms_per_batch);
                 if (run_kernel)
                     for (int s = 0; s < ns; s++) PV_KERNEL(nb, st[s]);
-                PV_CUDA(cudaDeviceSynchronize());
                 ctx->iterations_steady += (uint64_t)ns;
+                // With a fabric step, the launch that reaches the end of the
+                // burst is not waited for: the step is queued right behind
+                // it, so the GPU goes from burst to allreduce with no host
+                // round trip in between.
+                if (fabric && tl - b0 + launch_ns >= burst_ns) break;
+                PV_CUDA(cudaDeviceSynchronize());
+                launch_ns = gpl_mono_ns() - tl;
+            }
+            if (fabric) {
+                // The step goes on the first kernel stream (the tensor
+                // stream when there is no kernel), after every other stream's
+                // last work of the burst.
+                cudaStream_t s0 = run_kernel ? st[0] : ts.stream;
+                if (run_kernel)
+                    for (int s = 1; s < ns; s++) {
+                        PV_CUDA(cudaEventRecord(join[0], st[s]));
+                        PV_CUDA(cudaStreamWaitEvent(s0, join[0], 0));
+                    }
+                if (run_kernel && ts.active) {
+                    PV_CUDA(cudaEventRecord(join[1], ts.stream));
+                    PV_CUDA(cudaStreamWaitEvent(s0, join[1], 0));
+                }
+                PV_CHECK(gpl_fabric_step_enqueue(s0) == 0, "fabric step: enqueue failed");
+                PV_CUDA(cudaDeviceSynchronize());
+                gpl_fabric_step_record();
+                cycles_done++;
             }
             sleep_ms(a->duty_off_ms);
         } else {
@@ -369,6 +440,9 @@ int gpl_workload_powervirus_run(gpl_workload_ctx_t *ctx) {
 #undef PV_TENSOR
 
 cleanup:
+    gpl_fabric_step_free();
+    for (int i = 0; i < (int)(sizeof join / sizeof join[0]); i++)
+        if (join[i]) cudaEventDestroy(join[i]);
     tensor_stream_free(&ts);
     if (st) {
         for (int i = 0; i < ns; i++)

@@ -6,10 +6,9 @@
  *   - takes plain device pointers, sizes and a CUDA stream;
  *   - is stream-ordered (asynchronous: a device fault or a device-side
  *     wait timeout shows up at the caller's next sync and in
- *     gplk_status_read) and allocates nothing per call; the exceptions are
- *     named where they occur: gplk_fabric_create* allocate the fabric's
- *     buffers, and gplk_sgemm_f32 allocates a stream's stream-K workspace
- *     once, on that stream's first call that needs it;
+ *     gplk_status_read) and allocates no device memory; the one exception
+ *     is named where it occurs: gplk_fabric_create* allocate the fabric's
+ *     buffers;
  *   - returns a gplk_status code synchronously from argument and launch
  *     checks.
  *
@@ -40,7 +39,7 @@ typedef enum {
 const char *gplk_status_string(int status);
 
 /* ABI version: bumped when a signature or a data layout changes. */
-int gplk_abi_version(void);  /* 2: gplk_pv_cfg.budget_ns */
+int gplk_abi_version(void);  /* 3: gplk_sgemm_f32 takes beta and a workspace */
 
 /* Reads the device status word of the current device (first error recorded
  * by any gplk kernel since the last clear) and the site that recorded it.
@@ -74,17 +73,28 @@ int gplk_triad_f32_bulk(float *a, const float *b, const float *c, float s, size_
 int gplk_copy_f32(float *dst, const float *src, size_t n, cudaStream_t stream);
 
 /* ------------------------------------------------------------ SGEMM
- * C = A * B in true FP32 (SIMT FFMA, no TF32), row-major:
+ * C = A * B + beta * C in true FP32 (SIMT FFMA, no TF32), row-major:
  * A is M x K (leading dimension lda), B is K x N (ldb), C is M x N (ldc).
+ * beta = 0 never reads C; otherwise each output is fmaf(beta, C_old, A*B),
+ * which for beta = 1 is the sum rounded once.
  * Replaces cublasGemmEx with CUBLAS_COMPUTE_32F / CUBLAS_DEFAULT_MATH,
  * runner/src/workload_gemm.c:155-163, :174-179, :199-204 (column-major
- * C = A * B there, which is the row-major product C^T = B^T * A^T here).
- * Problems whose 128 x 128 tiles leave a wave of SMs ragged run stream-K
- * (a cooperative launch, one block per SM); the first such call on a stream
- * allocates that stream's workspace (64 KiB per SM, cudaMalloc), so it must
- * not be the first call on that stream inside a CUDA graph capture. */
-int gplk_sgemm_f32(const float *A, const float *B, float *C, int M, int N, int K, int lda,
-                   int ldb, int ldc, cudaStream_t stream);
+ * C = A * B there, beta 0, which is the row-major product C^T = B^T * A^T
+ * here), and the fp32 powervirus tensor stream's beta = 1 call,
+ * runner/src/workload_powervirus.cu:363-380.
+ * Problems whose 128 x 128 tiles leave a wave of SMs ragged run stream-K (a
+ * cooperative launch, one block per SM) in the caller's workspace of
+ * gplk_sgemm_workspace_bytes(M, N, K) bytes (16-byte aligned; 0 when the
+ * shape does not use stream-K on the current device). With no workspace,
+ * or a smaller one, the same product runs on whole tiles instead (the sums
+ * then differ by FP32 rounding order). The first call that sees a workspace
+ * zeroes its flags on `stream`; one workspace serves one stream at a time.
+ * After a GPLK_STATUS_DEVICE_TIMEOUT at site 0x0B01 (a stream-K partial
+ * that never arrived), zero the workspace before reusing it in a captured
+ * CUDA graph, or re-instantiate the graph. */
+size_t gplk_sgemm_workspace_bytes(int M, int N, int K);
+int gplk_sgemm_f32(const float *A, const float *B, float *C, int M, int N, int K, int lda, int ldb, int ldc,
+                   float beta, void *workspace, size_t workspace_bytes, cudaStream_t stream);
 
 /* ------------------------------------------------------------ FP8 GEMM
  * D = (*scale_a) * (*scale_b) * (A^T * B) with E4M3 operands, FP32
@@ -143,6 +153,20 @@ int gplk_gemm_tf32_nn(const float *A, const float *B, float *D, int M, int N, in
                       cudaStream_t stream);
 int gplk_gemm_i8_nn(const int8_t *A, const int8_t *B, int32_t *D, int M, int N, int K,
                     cudaStream_t stream);
+
+/* The same four with beta = 1: C = A * B + C in place (C is read, the
+ * product added in FP32 / S32, the sum rounded once to C's type; S32 wraps).
+ * Replaces the powervirus tensor stream's cublasGemmEx with beta = 1
+ * ("beta=1 keeps C live"), runner/src/workload_powervirus.cu:363-380, for
+ * bf16, fp16, tf32 and int8. Same layout and requirements as above. */
+int gplk_gemm_bf16_nn_acc(const uint16_t *A, const uint16_t *B, uint16_t *C, int M, int N, int K,
+                          cudaStream_t stream);
+int gplk_gemm_f16_nn_acc(const uint16_t *A, const uint16_t *B, uint16_t *C, int M, int N, int K,
+                         cudaStream_t stream);
+int gplk_gemm_tf32_nn_acc(const float *A, const float *B, float *C, int M, int N, int K,
+                          cudaStream_t stream);
+int gplk_gemm_i8_nn_acc(const int8_t *A, const int8_t *B, int32_t *C, int M, int N, int K,
+                        cudaStream_t stream);
 
 /* ------------------------------------------------------------ fabric step
  * The powervirus cycle's fabric step: an in-place BF16 sum allreduce across

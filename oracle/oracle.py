@@ -341,6 +341,11 @@ def ref_lib() -> ctypes.CDLL:
         L.ref_lt_ptrs.argtypes = [_p, _p]
         L.ref_gemm_ex.restype = _i
         L.ref_gemm_ex.argtypes = [_i, _p, _p, _p, _i, _p]
+        L.ref_ts_new.restype = _p
+        L.ref_ts_new.argtypes = [_i, _i]
+        L.ref_ts_ptrs.argtypes = [_p, _p]
+        L.ref_ts_enqueue.argtypes = [_p, _i]
+        L.ref_ts_delete.argtypes = [_p]
         _ref = L
     return _ref
 

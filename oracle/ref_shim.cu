@@ -83,4 +83,38 @@ void ref_lt_ptrs(void *gv, void **out) {
     out[4] = g->dScaleA; out[5] = g->dScaleB; out[6] = g->dScaleD;
 }
 
+// The powervirus rung's concurrent tensor stream (workload_powervirus.cu:
+// 281-397) for one non-Lt precision, as the rung sets it up:
+// tensor_stream_init allocates n x n A, B, C (0x3c fill; cuBLAS handle with
+// CUBLAS_TENSOR_OP_MATH), the test seeds them through ref_ts_ptrs, and
+// tensor_stream_enqueue issues `count` cublasGemmEx with beta = 1 (C += A*B).
+struct RefTs {
+    gpl_args_t args;
+    gpl_workload_ctx_t ctx;
+    gpl_tensor_stream_t ts;
+};
+void *ref_ts_new(int prec, int n) {
+    RefTs *r = (RefTs *)calloc(1, sizeof(RefTs));
+    gpl_args_defaults(&r->args);
+    r->args.precision = (gpl_prec_t)prec;
+    r->args.size = n;
+    r->ctx.args = &r->args;
+    if (tensor_stream_init(&r->ctx, &r->ts) != 0) {
+        tensor_stream_free(&r->ts);
+        free(r);
+        return NULL;
+    }
+    return r;
+}
+void ref_ts_ptrs(void *rv, void **out) {
+    RefTs *r = (RefTs *)rv;
+    out[0] = r->ts.dA; out[1] = r->ts.dB; out[2] = r->ts.dC; out[3] = (void *)r->ts.stream;
+}
+void ref_ts_enqueue(void *rv, int count) { tensor_stream_enqueue(&((RefTs *)rv)->ts, count); }
+void ref_ts_delete(void *rv) {
+    RefTs *r = (RefTs *)rv;
+    tensor_stream_free(&r->ts);
+    free(r);
+}
+
 }  // extern "C"

@@ -53,7 +53,7 @@ nvcc $NVFLAGS -I"$SRC" -c "$SRC/workload_nccl.cu" -o "$TMP/gplk/workload_nccl.o"
 for f in workload_gemm.c workload_util.c summary.c; do
     gcc $CFLAGS $INC -c "$DROP/$f" -o "$TMP/gplk/drop_${f%.c}.o"
 done
-for f in workload_memstream.cu workload_powervirus.cu; do
+for f in workload_memstream.cu workload_powervirus.cu fabric_step.cu; do
     nvcc $NVFLAGS $INC -c "$DROP/$f" -o "$TMP/gplk/drop_${f%.cu}.o"
 done
 nvcc $GEN -o "$OUT/gpu-power-runner-gplk" "$TMP"/gplk/*.o \

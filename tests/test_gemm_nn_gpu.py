@@ -141,3 +141,86 @@ def test_against_reference_cublas_rung(prec, n, gplk, oracle, cuda):
     print(f"{prec} n={n}: rel err gplk {e_ours:.2e}, reference {e_ref:.2e}")
     assert e_ours <= max(TOL[prec], 1.05 * e_ref)
     assert _rel(ours, theirs.astype(np.float64)) <= max(2 * TOL[prec], 2 * e_ref)
+
+
+def _old_d(prec: str, M: int, N: int, seed: int):
+    """(values as float64 / int64, device tensor) of a random old D."""
+    import torch
+
+    rng = np.random.default_rng(seed)
+    if prec == "i8":
+        v = rng.integers(-(1 << 31), 1 << 31, size=(N, M), dtype=np.int64).astype(np.int32)
+        return v.astype(np.int64), torch.from_numpy(v).cuda()
+    v = rng.uniform(-16.0, 16.0, size=(N, M)).astype(np.float32)
+    t = torch.from_numpy(v).to({"bf16": torch.bfloat16, "f16": torch.float16, "tf32": torch.float32}[prec])
+    return t.float().numpy().astype(np.float64), t.cuda()
+
+
+@pytest.mark.parametrize("prec", ["bf16", "f16", "tf32", "i8"])
+@pytest.mark.parametrize("shape", [(256, 256, 256), (1024, 1024, 1024), (264, 520, 128), (768, 1, 64),
+                                   (4352, 272, 64)], ids=lambda s: "x".join(map(str, s)))
+def test_accumulate_matches_oracle(prec, shape, gplk, oracle, cuda):
+    """beta = 1 (the tensor stream's C = A * B + C): the old D is read and the
+    product added before the single rounding; S32 wraps."""
+    import torch
+
+    M, N, K = shape
+    if prec == "i8" and (M % 16 or K % 16):
+        pytest.skip("i8 needs M, K multiples of 16")
+    a, b, ta, tb, _ = _inputs(prec, M, N, K, seed=M + 5 * N + K)
+    d0, td = _old_d(prec, M, N, seed=M * 3 + K)
+    gplk.gemm_nn(prec, ta, tb, td, M, N, K, accumulate=True)
+    torch.cuda.synchronize()
+    if prec == "i8":
+        want = ((oracle.gemm_nn_i8(a, b, M, N, K).astype(np.int64) + d0 + (1 << 31)) % (1 << 32) - (1 << 31))
+        assert np.array_equal(td.cpu().numpy().astype(np.int64), want)
+    else:
+        want = oracle.gemm_nn_f64(a, b, M, N, K) + d0
+        assert _rel(td.float().cpu().numpy(), want) <= TOL[prec], (prec, shape)
+
+
+@pytest.mark.parametrize("prec", ["bf16", "f16", "tf32", "i8"])
+def test_accumulate_vs_reference_tensor_stream(prec, gplk, oracle, cuda):
+    """The reference rung's own tensor stream (tensor_stream_init /
+    tensor_stream_enqueue, runner/src/workload_powervirus.cu:281-397, compiled
+    from that file): two beta = 1 GEMMs into the same C on the same operands.
+    INT8 bit-exact; otherwise libgplk at least as close to the
+    double-accumulated oracle as the reference (whose FP16 path accumulates in
+    FP16 under CUBLAS_TENSOR_OP_MATH)."""
+    import torch
+
+    from gplk.lt import device_view
+
+    if not oracle.ref_available():
+        pytest.skip("reference library not built")
+    n = 1024
+    a, b, ta, tb, _ = _inputs(prec, n, n, n, seed=77)
+    d0, td = _old_d(prec, n, n, seed=78)
+    ref_c = td.clone()
+    for _ in range(2):
+        gplk.gemm_nn(prec, ta, tb, td, n, n, n, accumulate=True)
+    L = oracle.ref_lib()
+    r = L.ref_ts_new(GPL_PREC[prec], n)
+    assert r, "reference tensor stream set-up failed"
+    try:
+        ptrs = (ctypes.c_void_p * 4)()
+        L.ref_ts_ptrs(r, ptrs)
+        nb_in, nb_out = ta.numel() * ta.element_size(), ref_c.numel() * ref_c.element_size()
+        device_view(ptrs[0], nb_in).copy_(ta.view(-1).view(torch.uint8))
+        device_view(ptrs[1], nb_in).copy_(tb.view(-1).view(torch.uint8))
+        device_view(ptrs[2], nb_out).copy_(ref_c.view(-1).view(torch.uint8))
+        torch.cuda.synchronize()
+        L.ref_ts_enqueue(r, 2)
+        torch.cuda.synchronize()
+        theirs_t = device_view(ptrs[2], nb_out).clone().view(ref_c.dtype).view(n, n)
+    finally:
+        L.ref_ts_delete(r)
+    torch.cuda.synchronize()
+    if prec == "i8":
+        assert torch.equal(td, theirs_t)
+        return
+    want = 2.0 * oracle.gemm_nn_f64(a, b, n, n, n) + d0
+    e_ours = _rel(td.float().cpu().numpy(), want)
+    e_ref = _rel(theirs_t.float().cpu().numpy(), want)
+    print(f"{prec} beta=1 x2: rel err gplk {e_ours:.2e}, reference tensor stream {e_ref:.2e}")
+    assert e_ours <= max(TOL[prec], 1.05 * e_ref)

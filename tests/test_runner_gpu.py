@@ -89,15 +89,18 @@ def test_powervirus_default_mix(tmp_path):
 
 
 @needs_runner
-@pytest.mark.parametrize("prec", ["fp8", "fp4", "bf16", "int8"])
-def test_powervirus_tensor_stream_narrow_formats(prec, tmp_path):
-    """--tensor-backend cublas: GEMMs on a concurrent stream through libgplk's
-    tcgen05 GEMMs (gpl_lt_* for fp8/fp4, the NN kernels for bf16/int8).
-    Tensor-only, so FLOPs are counted."""
+@pytest.mark.parametrize("prec,min_tflops", [("fp8", 1000.0), ("fp4", 1000.0), ("bf16", 700.0), ("int8", 1000.0),
+                                             ("fp16", 700.0), ("tf32", 350.0), ("fp32", 20.0), ("fp64", 1.0)])
+def test_powervirus_tensor_stream(prec, min_tflops, tmp_path):
+    """--tensor-backend cublas: GEMMs on a concurrent stream, tensor-only (so
+    FLOPs are counted): gpl_lt_* for fp8/fp4, the tcgen05 NN kernels with
+    beta = 1 for bf16/fp16/tf32/int8, the SIMT SGEMM with beta = 1 for fp32,
+    cublasGemmEx with beta = 1 for fp64."""
+    size = "8192" if prec not in ("fp32", "fp64") else "2048"
     res, s, _ = run_rung(GPLK_RUNNER, tmp_path, "--op", "powervirus", "--tensor-backend", "cublas",
-                         "--precision", prec, "--size", "8192", "--mix-fma", "0", "--mix-dram", "0")
+                         "--precision", prec, "--size", size, "--mix-fma", "0", "--mix-dram", "0")
     _ok(res, s)
-    assert s["compute"]["tflops_measured"] > 1000.0
+    assert s["compute"]["tflops_measured"] > min_tflops
 
 
 @needs_runner
@@ -180,17 +183,79 @@ def test_powervirus_summary_extended_contract_and_violation_units(tmp_path):
 
 
 @needs_runner
-def test_gemm_backend_switch_keeps_cublas(tmp_path):
-    """GPL_GEMM_BACKEND=cublas runs the bf16 rung on cublasGemmEx, as the
-    reference does; the default runs it on the tcgen05 kernel."""
-    res, s, _ = run_rung(GPLK_RUNNER, tmp_path, "--op", "sgemm", "--precision", "bf16", "--size", "4096",
-                         env={"GPL_GEMM_BACKEND": "cublas"})
-    _ok(res, s)
-    assert s["compute"]["tflops_measured"] > 300.0
-
-
-@needs_runner
 def test_tc_gemm_rejects_unaligned_size_with_hint(tmp_path):
     res, s, _ = run_rung(GPLK_RUNNER, tmp_path, "--op", "sgemm", "--precision", "int8", "--size", "1000")
     assert res.returncode == 5
-    assert s["result"] == "cuda_error" and "GPL_GEMM_BACKEND=cublas" in s.get("error_message", "")
+    assert s["result"] == "cuda_error" and "multiple of" in s.get("error_message", "")
+
+
+@needs_runner
+@pytest.mark.parametrize("impl", ["gplk", "nccl"])
+def test_powervirus_fabric_step_single_rank(impl, tmp_path):
+    """The duty cycle with its per-cycle BF16 allreduce (GPL_FABRIC) on one
+    rank: every cycle ends with the step, the summary's transient block
+    reports it, and the extended schema accepts the document."""
+    from gplk import summary as S
+
+    d = tmp_path / "rdv"
+    d.mkdir()
+    env = {"GPL_FABRIC": impl, "GPL_FABRIC_WORLD": "1", "GPL_FABRIC_RANK": "0", "GPL_FABRIC_DIR": str(d),
+           "GPL_FABRIC_MIB": "64", "GPL_PV_BUDGET_US": "1000"}
+    res, s, _ = run_rung(GPLK_RUNNER, tmp_path, "--op", "powervirus", "--size", "4096", "--mix-tensor", "2",
+                         "--duty-on-ms", "100", "--duty-off-ms", "100", env=env)
+    _ok(res, s)
+    f = s["transient"]["fabric"]
+    assert f["impl"] == impl and f["world"] == 1 and f["rank"] == 0 and f["bytes"] == 64 << 20
+    assert f["cycles"] == 10  # 2 s steady / 200 ms period
+    assert 0.0 < f["median_ms"] <= f["max_ms"] < 100.0
+    S.validate_doc(s)
+
+
+@needs_runner
+def test_powervirus_fabric_step_rejects_fixed_work(tmp_path):
+    d = tmp_path / "rdv"
+    d.mkdir()
+    env = {"GPL_FABRIC": "gplk", "GPL_FABRIC_WORLD": "1", "GPL_FABRIC_RANK": "0", "GPL_FABRIC_DIR": str(d)}
+    res, s, _ = run_rung(GPLK_RUNNER, tmp_path, "--op", "powervirus", "--size", "1024", "--iters", "8",
+                         "--duty-on-ms", "100", "--duty-off-ms", "100", env=env)
+    assert res.returncode == 5
+    assert s["result"] == "cuda_error" and "fixed work" in s.get("error_message", "")
+
+
+def _gpus() -> int:
+    try:
+        import torch
+
+        return torch.cuda.device_count()
+    except Exception:
+        return 0
+
+
+@needs_runner
+@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("impl", ["gplk", "nccl"])
+def test_powervirus_fabric_step_two_ranks(impl, tmp_path):
+    """Two runner processes, one per GPU, in phase: the same number of
+    cycles on both, each cycle ending in the 2-rank allreduce."""
+    d = tmp_path / "rdv"
+    d.mkdir()
+    procs, outs = [], []
+    for r in range(2):
+        out = tmp_path / f"r{r}"
+        out.mkdir()
+        env = dict(os.environ, GPL_FABRIC=impl, GPL_FABRIC_WORLD="2", GPL_FABRIC_RANK=str(r), GPL_FABRIC_DIR=str(d),
+                   GPL_FABRIC_MIB="256", GPL_PV_BUDGET_US="1000", NCCL_NVLS_ENABLE="0")
+        cmd = [str(GPLK_RUNNER), "--warmup-sec", "1", "--steady-sec", "2", "--sample-hz", "50", "--device", str(r),
+               "--out-summary", str(out / "summary.json"), "--out-metrics", str(out / "metrics.ndjson"),
+               "--op", "powervirus", "--size", "4096", "--mix-tensor", "2", "--duty-on-ms", "100",
+               "--duty-off-ms", "100"]
+        procs.append(subprocess.Popen(cmd, env=env, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True))
+        outs.append(out)
+    for p in procs:
+        _, err = p.communicate(timeout=300)
+        assert p.returncode == 0, err[-2000:]
+    sums = [json.loads((o / "summary.json").read_text()) for o in outs]
+    fs = [s["transient"]["fabric"] for s in sums]
+    assert [f["rank"] for f in fs] == [0, 1] and all(f["world"] == 2 for f in fs)
+    assert fs[0]["cycles"] == fs[1]["cycles"] == 10
+    assert all(f["busbw_gbs"] > 50.0 for f in fs)

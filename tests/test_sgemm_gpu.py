@@ -147,3 +147,51 @@ def test_sgemm_stream_k_repeatable_and_per_stream(gplk, oracle, cuda):
     assert _rel_fro(got[1], want[1]) <= TOL
     assert np.array_equal(got[0], got[2]) and np.array_equal(got[0], got[3])
     assert gplk.status_read() == (0, 0)
+
+
+# beta = 1 (C = A B + C, the fp32 powervirus tensor stream's call) on every
+# kernel family: stream-K (1024^3, 1000 x 1000 x 333), whole tiles (2048 x
+# 2304 x 300), the register-staged kernels (100 x 130 x 257, unaligned), and
+# the split-K cluster pair (257 x 129 x 1000).
+@pytest.mark.parametrize("mnk", [(1024, 1024, 1024), (1000, 1000, 333), (2048, 2304, 300), (100, 130, 257),
+                                 (257, 129, 1000), (33, 17, 5)])
+@pytest.mark.parametrize("beta", [1.0, 0.5])
+def test_sgemm_beta(mnk, beta, gplk, oracle, cuda):
+    import torch
+
+    M, N, K = mnk
+    A = oracle.uniform_f32(M * K, seed=M + 1, lo=-1.0, hi=1.0).reshape(M, K)
+    B = oracle.uniform_f32(K * N, seed=N + 2, lo=-1.0, hi=1.0).reshape(K, N)
+    C0 = oracle.uniform_f32(M * N, seed=K + 3, lo=-8.0, hi=8.0).reshape(M, N)
+    C = torch.from_numpy(C0).to(cuda)
+    gplk.sgemm(torch.from_numpy(A).to(cuda), torch.from_numpy(B).to(cuda), C, beta=beta)
+    torch.cuda.synchronize()
+    want = oracle.sgemm_f64acc(A, B) + beta * C0.astype(np.float64)
+    assert _rel_fro(C.cpu().numpy(), want) <= TOL, mnk
+
+
+def test_sgemm_workspace_optional(gplk, oracle, cuda):
+    """A stream-K shape with the caller's workspace, with none, and with one
+    too small (the whole-tile kernel then runs): all within the tolerance;
+    no workspace and a too-small one take the same kernel, bit for bit."""
+    import torch
+
+    n = 1024
+    assert gplk.sgemm_workspace_bytes(n, n, n) > 0        # 64 tiles on 148 SMs: stream-K
+    assert gplk.sgemm_workspace_bytes(4096, 4096, 4096) == 0  # whole waves: no workspace
+    A = oracle.uniform_f32(n * n, seed=0, lo=-1.0, hi=1.0).reshape(n, n)
+    B = oracle.uniform_f32(n * n, seed=1, lo=-1.0, hi=1.0).reshape(n, n)
+    tA, tB = torch.from_numpy(A).to(cuda), torch.from_numpy(B).to(cuda)
+    want = oracle.sgemm_f64acc(A, B)
+    ws = torch.empty(gplk.sgemm_workspace_bytes(n, n, n), dtype=torch.uint8, device=cuda)
+    small = torch.empty(4096, dtype=torch.uint8, device=cuda)
+    outs = [torch.full((n, n), float("nan"), device=cuda) for _ in range(3)]
+    gplk.sgemm(tA, tB, outs[0], workspace=ws)
+    gplk.sgemm(tA, tB, outs[1], workspace=None)
+    gplk.sgemm(tA, tB, outs[2], workspace=small)
+    torch.cuda.synchronize()
+    got = [o.cpu().numpy() for o in outs]
+    for g in got:
+        assert _rel_fro(g, want) <= TOL
+    assert np.array_equal(got[1], got[2])
+    assert gplk.status_read() == (0, 0)
