@@ -91,10 +91,14 @@ __global__ void __launch_bounds__(kBulkThreads) triad_bulk(float* __restrict__ a
     __syncthreads();
     const bool ok = mbar_wait(&full, 0, &abort_flag, 0x0101);
     if (__syncthreads_or(!ok)) {
-        // Give up together; let the copies this block issued land first.
+        // Give up together. The copies this block issued write into its
+        // shared memory, so the block stays resident until they have landed:
+        // up to 20 further bounded waits of 100 ms (a bulk copy from valid
+        // global memory always completes; each wait that runs out is recorded).
         if (threadIdx.x == 0) {
             int dummy = 0;
-            mbar_wait(&full, 0, &dummy, 0x0102, 100000000ull);
+            for (int tries = 0; tries < 20 && !mbar_wait(&full, 0, &dummy, 0x0102, 100000000ull); ++tries) {
+            }
         }
         __syncthreads();
         return;

@@ -15,16 +15,16 @@
 // the sink. Every GPU that loads libgplk holds the array until the process
 // exits.
 //
-// Set-up: the first call on each device, with that device current, looks up
-// the array's device address with cudaGetSymbolAddress (the array's name in
-// host code is only a host-side stand-in, never a device address) and fills
-// the streaming window with a byte pattern, then synchronises the caller's
-// stream once. Make that first call before any stream capture.
-// Every call clears the sink before launching, because the atomics of the
-// previous call leave their counts in it. All calls share the array: calls
-// that overlap on the GPU (other streams, other threads) race on the sink.
+// Every call, with the caller's device current, looks up the array's device
+// address on that device with cudaGetSymbolAddress (the array's name in host
+// code is only a host-side stand-in, never a device address), then, ordered
+// on the caller's stream, fills the requested streaming window with a byte
+// pattern and clears the sink (the atomics of the previous call leave their
+// counts in it) before the launch. Nothing is cached between calls, so a
+// call never uses an address or contents left from before a cudaDeviceReset,
+// and no call synchronises. All calls share the array: calls that overlap on
+// the GPU (other streams, other threads) race on the window and the sink.
 #include <cstdio>
-#include <mutex>
 
 #include "gplk_ptx.cuh"
 
@@ -38,31 +38,14 @@ constexpr unsigned char kStreamPattern = 0x3c;
 
 static __device__ __align__(256) unsigned char g_pv_scratch[kScratchBytes];
 
-struct DeviceScratch {
-    unsigned char* base = nullptr;  // device address of g_pv_scratch on this device
-    bool ready = false;
-};
-
-static DeviceScratch g_dev_scratch[64];
-static std::mutex g_dev_scratch_mu;
-
-// Once per device, with the device current: resolve the device address and
-// fill the streaming window.
-static int device_scratch(int dev, cudaStream_t stream, unsigned char** base) {
-    std::lock_guard<std::mutex> lock(g_dev_scratch_mu);
-    DeviceScratch& s = g_dev_scratch[dev];
-    if (!s.ready) {
-        void* p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_pv_scratch) != cudaSuccess || p == nullptr)
-            return GPLK_STATUS_CUDA_ERROR;
-        unsigned char* b = static_cast<unsigned char*>(p);
-        if (cudaMemsetAsync(b + kSinkBytes, kStreamPattern, kMaxStreamBytes, stream) != cudaSuccess ||
-            cudaStreamSynchronize(stream) != cudaSuccess)
-            return GPLK_STATUS_CUDA_ERROR;
-        s.base = b;
-        s.ready = true;
+// The array's device address on the current device.
+static int device_scratch(unsigned char** base) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_pv_scratch) != cudaSuccess || p == nullptr) {
+        cudaGetLastError();
+        return GPLK_STATUS_CUDA_ERROR;
     }
-    *base = s.base;
+    *base = static_cast<unsigned char*>(p);
     return GPLK_STATUS_OK;
 }
 
@@ -93,7 +76,7 @@ extern "C" int gplk_powervirus_launch_noalloc(const unsigned char* role_map, siz
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return GPLK_STATUS_CUDA_ERROR;
     unsigned char* base = nullptr;
-    st = nz::device_scratch(dev, stream, &base);
+    st = nz::device_scratch(&base);
     if (st != GPLK_STATUS_OK) return st;
     static thread_local uint64_t configured = 0;
     if (!(configured & (1ull << dev))) {
@@ -101,8 +84,11 @@ extern "C" int gplk_powervirus_launch_noalloc(const unsigned char* role_map, siz
             return GPLK_STATUS_LAUNCH_FAIL;
         configured |= 1ull << dev;
     }
-    // The sink starts every call at zero, as a freshly cleared caller sink would.
-    if (cudaMemsetAsync(base, 0, nz::kSinkBytes, stream) != cudaSuccess) return GPLK_STATUS_CUDA_ERROR;
+    // The window holds the pattern a caller's buffer would be filled with, and
+    // the sink starts at zero, as a freshly cleared caller sink would.
+    if (cudaMemsetAsync(base + nz::kSinkBytes, nz::kStreamPattern, stream_bytes, stream) != cudaSuccess ||
+        cudaMemsetAsync(base, 0, nz::kSinkBytes, stream) != cudaSuccess)
+        return GPLK_STATUS_CUDA_ERROR;
     pv::Params p;
     p.role_map = role_map;
     p.stream_buf = reinterpret_cast<const float4*>(base + nz::kSinkBytes);

@@ -18,7 +18,12 @@
  *              VEC16_UE4M3 layout (gplk_nvfp4_sf_bytes(n, n) bytes each)
  *   dAlpha     FP32 global scale product (D = alpha * sum sfa*a*sfb*b)
  * The cuBLASLt handle/descriptor members are gone; `ready`, `n`, `prec`,
- * `stream`, `workspace_bytes` keep their meaning (no workspace is needed).
+ * `stream` keep their meaning. `workspace` / `workspace_bytes` hold K-padded
+ * copies of the operands when n is not a multiple of 16 (FP8) or 256 (FP4);
+ * each enqueue then refreshes them from dA / dB / dSFA / dSFB first.
+ * The struct's layout differs from the reference's (whose cuBLASLt members
+ * come first), so the drop-in is source-compatible: callers rebuild against
+ * this header; code that touches only the named fields is unchanged.
  */
 #ifndef GPL_GEMM_LT_H
 #define GPL_GEMM_LT_H
@@ -70,8 +75,9 @@ bool gpl_lt_precision_supported(gpl_prec_t p);
 
 /* Allocates the n x n problem, fills A and B with 0x38 (E4M3 1.0; FP4 pair
  * -0 / 1.5), zeroes C, sets the scales (and FP4 block scales) to 1.0.
- * Returns 0, or -1 with a logged reason (bad precision, n not a multiple of
- * 256 for FP4, out of memory, device not sm_100).
+ * FP8 takes any n > 0, as the reference does; FP4 any multiple of 32.
+ * Returns 0, or -1 with a logged reason (bad precision, an FP4 n that is not
+ * a multiple of 32, out of memory, device not sm_100).
  * Replaces runner/src/gemm_lt.cu:57-161. */
 int gpl_lt_init(gpl_lt_gemm_t *g, gpl_prec_t prec, int n, cudaStream_t stream);
 

@@ -186,7 +186,9 @@ int gplk_gemm_i8_nn_acc(const int8_t *A, const int8_t *B, int32_t *C, int M, int
  * elements (a multiple of 8) are summed in FP32 in rank order and rounded
  * once to BF16, in every rank's buffer. A rank that does not arrive within
  * 2 s makes the others return with GPLK_STATUS_DEVICE_TIMEOUT in the status
- * word (gplk_status_read). world <= 8. */
+ * word (gplk_status_read). world <= 8. After such a timeout the ranks may
+ * disagree on the fabric's epoch: destroy the fabric on every rank and
+ * create a new one; do not reuse it. */
 typedef struct gplk_fabric gplk_fabric;
 size_t gplk_fabric_handle_bytes(void);
 int gplk_fabric_create(int rank, int world, size_t bytes, gplk_fabric **out, void *handle);
@@ -274,11 +276,13 @@ int gplk_pv_block_threads(void);
  * GPLK_STATUS_BAD_ARG and a message on stderr. A 32 MiB window fits in L2,
  * so in this variant the DRAM role streams mostly from L2, not HBM.
  *
- * The first call on a device (with that device current) resolves the
- * array's address, fills the window with the byte 0x3c and synchronises
- * `stream`; make it before any stream capture. Each call zeroes the sink.
- * All calls share the array, so calls that overlap on the GPU race on it.
- * Allocates nothing: no cudaMalloc, cudaFree or allocating library call. */
+ * Every call, with the device current, resolves the array's device address
+ * on that device and, ordered on `stream` before the launch, fills the window
+ * with the byte 0x3c and zeroes the sink. Nothing is cached between calls
+ * (the entry point stays valid after a cudaDeviceReset) and no call
+ * synchronises. All calls share the array, so calls that overlap on the GPU
+ * race on it. Allocates nothing: no cudaMalloc, cudaFree or allocating
+ * library call. */
 #define GPLK_PV_NOALLOC_MAX_STREAM_BYTES ((size_t)32 << 20)
 int gplk_powervirus_launch_noalloc(const unsigned char *role_map, size_t stream_bytes, int blocks,
                                    int inner, float *verify_out, const uint8_t *mma_a,

@@ -170,3 +170,106 @@ def test_init_seeds_reference_fill(gplk, cuda):
         assert bool((d == float(n)).all())
     finally:
         lt.lt_free(g)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n", [1000, 1001, 136])
+def test_fp8_any_n_through_padded_path(n, gplk, oracle, cuda):
+    """The reference takes any n (runner/src/gemm_lt.cu:57-161); sizes the
+    kernel cannot read directly (K % 16 != 0) run on K-padded copies that
+    every enqueue refreshes from the public dA / dB. Checked against the CPU
+    oracle over all of D, and against the reference's own gpl_lt path."""
+    import torch
+    from gplk import lt
+
+    a = oracle.normal_f32(n * n, n + 5).reshape(n, n)
+    b = oracle.normal_f32(n * n, n + 6).reshape(n, n)
+    qa, sa = oracle.quantize_fp8(a)
+    qb, sb = oracle.quantize_fp8(b)
+    tA, tB = torch.from_numpy(qa).to(cuda), torch.from_numpy(qb).to(cuda)
+    sc = torch.tensor([sa, sb], dtype=torch.float32, device=cuda)
+    g = lt.LtGemm()
+    lt.lt_init(g, lt.PREC_FP8, n)
+    try:
+        assert (g.workspace is not None) == (n % 16 != 0)
+        _seed(lt.device_view(g.dA, n * n), tA)
+        _seed(lt.device_view(g.dB, n * n), tB)
+        lt.device_view(g.dScaleA, 1, "<f4").copy_(sc[:1])
+        lt.device_view(g.dScaleB, 1, "<f4").copy_(sc[1:])
+        lt.lt_enqueue(g, 1)
+        torch.cuda.synchronize()
+        ours = lt.device_view(g.dD, n * n, "<i2").view(torch.bfloat16).float().cpu().numpy().reshape(n, n)
+        # a rewrite of dA between enqueues is seen by the next one
+        lt.device_view(g.dA, n * n).zero_()
+        lt.lt_enqueue(g, 1)
+        torch.cuda.synchronize()
+        zero = lt.device_view(g.dD, n * n, "<i2").view(torch.bfloat16).float()
+        assert bool((zero == 0).all())
+    finally:
+        lt.lt_free(g)
+    want = oracle.gemm_fp8_tn(qa, qb, sa, sb)
+    assert _rel_fro(ours, want) <= TOL
+    if oracle.ref_available():
+        L = oracle.ref_lib()
+        r = L.ref_lt_new()
+        if L.gpl_lt_init(r, oracle.PREC["fp8"], n, torch.cuda.current_stream().cuda_stream) != 0:
+            # cuBLASLt finds no FP8 algorithm for this n (odd leading
+            # dimensions): the reference cannot run it at all.
+            L.ref_lt_delete(r)
+            assert n % 16 != 0
+            return
+        try:
+            ptrs = (ctypes.c_void_p * 7)()
+            L.ref_lt_ptrs(r, ptrs)
+            torch.cuda.synchronize()
+            _seed(lt.device_view(ptrs[0], n * n), tA)
+            _seed(lt.device_view(ptrs[1], n * n), tB)
+            lt.device_view(ptrs[4], 1, "<f4").copy_(sc[:1])
+            lt.device_view(ptrs[5], 1, "<f4").copy_(sc[1:])
+            torch.cuda.synchronize()
+            rc = L.gpl_lt_enqueue(r, 1)
+            torch.cuda.synchronize()
+            if rc == 0:
+                ref = lt.device_view(ptrs[3], n * n, "<i2").view(torch.bfloat16).float().cpu().numpy()
+                assert _rel_fro(ours, ref.reshape(n, n)) <= TOL
+        finally:
+            L.gpl_lt_free(r)
+            L.ref_lt_delete(r)
+
+
+@pytest.mark.gpu
+def test_fp4_padded_k_and_rejected_size(gplk, oracle, cuda):
+    """NVFP4 at n = 2080 (a multiple of 32, not of 256) through the padded
+    path, against the CPU oracle on sampled entries; n = 1000 (rows not on
+    16-byte boundaries) is refused with -1."""
+    import torch
+    from gplk import lt
+
+    g = lt.LtGemm()
+    with pytest.raises(gplk.GplkError):
+        lt.lt_init(g, lt.PREC_FP4, 1000)
+    n = 2080
+    a = oracle.normal_f32(n * n, 17).reshape(n, n)
+    b = oracle.normal_f32(n * n, 18).reshape(n, n)
+    pa, sfa, ga = oracle.quantize_nvfp4(a)
+    pb, sfb, gb = oracle.quantize_nvfp4(b)
+    t = lambda x: torch.from_numpy(np.ascontiguousarray(x)).to(cuda)  # noqa: E731
+    g = lt.LtGemm()
+    lt.lt_init(g, lt.PREC_FP4, n)
+    try:
+        assert g.workspace is not None
+        sfn = gplk.nvfp4_sf_bytes(n, n)
+        _seed(lt.device_view(g.dA, n * n // 2), t(pa))
+        _seed(lt.device_view(g.dB, n * n // 2), t(pb))
+        _seed(lt.device_view(g.dSFA, sfn), t(sfa))
+        _seed(lt.device_view(g.dSFB, sfn), t(sfb))
+        lt.device_view(g.dAlpha, 1, "<f4").fill_(ga * gb)
+        lt.lt_enqueue(g, 1)
+        torch.cuda.synchronize()
+        ours = lt.device_view(g.dD, n * n, "<i2").view(torch.bfloat16).float().cpu().numpy().reshape(n, n)
+    finally:
+        lt.lt_free(g)
+    rng = np.random.default_rng(9)
+    pairs = np.stack([rng.integers(0, n, 4096), rng.integers(0, n, 4096)], axis=1)
+    want = oracle.gemm_nvfp4_tn(pa, pb, sfa, sfb, n, ga * gb, pairs)
+    assert _rel_fro(ours[pairs[:, 1], pairs[:, 0]], want) <= TOL
