@@ -90,6 +90,9 @@ def parse_args():
                     help="memstream at N=1: skip the FP8 / NVFP4 GEMM and power rungs added to the line")
     ap.add_argument("--rung-seconds", type=float, default=1.5,
                     help="sustained run per GEMM rung arm (the power rung runs twice as long)")
+    ap.add_argument("--pv-cycle", action="store_true",
+                    help="memstream at N>1: also run a short in-phase powervirus duty cycle with the gplk fabric "
+                         "step and add its node power and fabric time to the line")
     ap.add_argument("--no-fabric-check", action="store_true",
                     help="memstream at N>1: skip the fabric step's parity check and timing added to the line")
     ap.add_argument("--elements", type=int, default=TRIAD_N,
@@ -515,6 +518,165 @@ def bench_gemm(args, dist: Dist) -> dict:
 
         dtype, workload = "f32", f"FP32 SGEMM C = A*B row-major, M=N=K={n}, U[-1,1)"
         launches_per_step = 2
+    else:
+        n = args.gemm_n or (16384 if w == "nvfp4" else 8192)
+        case = _gemm_case(w, n, dev, stream, seed=31 + 7 * dist.rank)
+        step = case["ours"]
+        dtype, workload = case["dtype"], case["workload"]
+        launches_per_step = 1
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(dist.local)
+    dist.barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    sampler.stop()
+    ms = e0.elapsed_time(e1)
+    ms_max = dist.max(ms)
+    code, site = gplk.status_read()
+    if code != 0:
+        raise RuntimeError(f"device status {code} at {site:#x}")
+
+    per_launch_s = ms / 1e3 / args.steps
+    achieved = nbytes / per_launch_s / 1e9
+    peaks = measured_peaks()
+    value = dist.world * nbytes * args.steps / (ms_max / 1e3) / 1e9
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = memstream_e2e(a, b, c, stream, bulk, dist, steps=3)
+    if n != TRIAD_N:
+        workload = f"memstream STREAM triad a = b + 3.0*c, FP32, 3 x {n} elements (profiling case)"
+    else:
+        workload = "memstream STREAM triad a = b + 3.0*c, FP32, 3 x 2^30 elements (4 GiB each)"
+
+    traffic = NCU_TRAFFIC["memstream_bulk" if bulk else "memstream_vec4"] if n == TRIAD_N else None
+    out = {
+        "metric": "memstream triad GB/s",
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": dist.world,
+        "steps": args.steps,
+        "warmup": max(args.warmup, 3),
+        "ms_per_step": round(ms_max / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic: b, c ~ U[0,1) from torch's seeded generator, s = 3.0",
+        "config": {"workload": workload,
+                   "elements": n, "bytes_per_step_per_gpu": nbytes,
+                   "kernel": "triad_bulk" if bulk else "triad_vec4",
+                   "l2": "inputs (12 GiB per step) larger than the 126 MB L2; no flush",
+                   "parallelism": f"replicas x{dist.world} (the workload does not shard)"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
+                     "peak_source": f"{peaks['_source']} hbm_gbs (burst copy)",
+                     "algorithmic_bytes_per_launch": nbytes},
+        "clocks": sampler.summary(),
+        "gpu_launches": args.steps,
+    }
+    if e2e:
+        out["e2e"] = e2e
+    return out
+
+
+def memstream_e2e(a, b, c, stream, bulk, dist: Dist, steps: int, chunk: int = 1 << 24) -> dict:
+    """The same triad through the C ABI with host buffers: every step copies
+    b and c from pinned host memory, runs the triad and reads a back, all of
+    it. The arrays move in chunks of `chunk` elements on three streams
+    (copy in, triad, copy out), so the host-to-device copies of later chunks
+    overlap the device-to-host copies of earlier ones: PCIe carries both
+    directions at once. Events keep every chunk's order: a chunk is
+    overwritten only after the previous step's triad read it, and a is
+    rewritten only after the previous step copied it out."""
+    import torch
+    import gplk
+
+    n = b.numel()
+    hb = torch.empty(n, dtype=torch.float32, pin_memory=True)
+    hc = torch.empty(n, dtype=torch.float32, pin_memory=True)
+    ha = torch.empty(n, dtype=torch.float32, pin_memory=True)
+    hb.copy_(b, non_blocking=False)
+    hc.copy_(c, non_blocking=False)
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    bounds = [(k, min(k + chunk, n)) for k in range(0, n, chunk)]
+    ev_in = [torch.cuda.Event() for _ in bounds]
+    ev_tr = [torch.cuda.Event() for _ in bounds]
+    ev_out = [torch.cuda.Event() for _ in bounds]
+    first = [True]
+
+    def step():
+        for i, (lo, hi) in enumerate(bounds):
+            if not first[0]:
+                s_in.wait_event(ev_tr[i])  # the previous step's triad has read b, c here
+            with torch.cuda.stream(s_in):
+                b[lo:hi].copy_(hb[lo:hi], non_blocking=True)
+                c[lo:hi].copy_(hc[lo:hi], non_blocking=True)
+                ev_in[i].record(s_in)
+            stream.wait_event(ev_in[i])
+            if not first[0]:
+                stream.wait_event(ev_out[i])  # the previous step has copied a out of here
+            gplk.triad(a[lo:hi], b[lo:hi], c[lo:hi], TRIAD_S, stream=stream, bulk=bulk)
+            ev_tr[i].record(stream)
+            s_out.wait_event(ev_tr[i])
+            with torch.cuda.stream(s_out):
+                ha[lo:hi].copy_(a[lo:hi], non_blocking=True)
+                ev_out[i].record(s_out)
+        first[0] = False
+
+    step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s_in)
+    for _ in range(steps):
+        step()
+    s_out.wait_event(ev_tr[-1])
+    e1.record(s_out)  # after the last copy out, which follows every chunk's triad
+    torch.cuda.synchronize()
+    ms = dist.max(e0.elapsed_time(e1))
+    value = dist.world * 12 * n * steps / (ms / 1e3) / 1e9
+    return {"value": round(value, 2), "unit": "GB/s", "h2d_bytes_per_step": 8 * n,
+            "d2h_bytes_per_step": 4 * n, "steps": steps,
+            "note": f"pinned host b, c -> device, triad, device a -> pinned host, per step, in "
+                    f"{len(bounds)} chunks on three streams (copy in / triad / copy out overlap)"}
+
+
+# ------------------------------------------------------------ GEMM rungs
+
+def bench_gemm(args, dist: Dist) -> dict:
+    import torch
+    import gplk
+
+    dev = torch.device("cuda", dist.local)
+    torch.cuda.set_device(dev)
+    gplk.lib()
+    g = torch.Generator(device=dev)
+    g.manual_seed(7 + dist.rank)
+    stream = torch.cuda.current_stream(dev)
+    w = args.workload
+    if w == "sgemm":
+        n = args.sgemm_n
+        A = torch.rand(n, n, device=dev, generator=g) * 2 - 1
+        B = torch.rand(n, n, device=dev, generator=g) * 2 - 1
+        C = torch.empty(n, n, device=dev)
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+        def step():
+            flush.zero_()  # 256 MiB write: evicts the 12 MiB working set from L2
+            gplk.sgemm(A, B, C, stream=stream)
+
+        dtype, workload = "f32", f"FP32 SGEMM C = A*B row-major, M=N=K={n}, U[-1,1)"
+        launches_per_step = 2
     elif w in NN_GEMMS:
         n = args.gemm_n or 8192
         if w == "i8":
@@ -617,6 +779,7 @@ def bench_gemm(args, dist: Dist) -> dict:
                      **({"scalar_ffma_measured": scalar_ffma} if scalar_ffma is not None else {})},
         "clocks": sampler.summary(),
         "gpu_launches": args.steps * (1 if w != "sgemm" else 1),
+        **(_sustained_extras(case, stream, dev, args.rung_seconds) if w != "sgemm" else {}),
     }
 
 
@@ -733,97 +896,159 @@ def _rel_frob(a, b) -> float:
     return float((a - b).norm() / b.norm().clamp_min(1e-30))
 
 
-def rung_gemm(kind: str, dev, stream, seconds: float) -> dict:
-    """FP8 E4M3 8192^3 or NVFP4 16384^3 on N(0,1) operands quantised as the
-    rung configuration states (gplk.operands), through the C ABI; the same
-    operands through cuBLASLt (torch's scaled matmul) on the same GPU beside
-    it; and the GEMM end to end with host operands."""
+def _gemm_case(kind: str, n: int, dev, stream, seed: int = 31) -> dict:
+    """One square tensor-core GEMM of the ladder on configured operands:
+    fp8 / nvfp4 from N(0,1) quantised as the rung configuration states
+    (gplk.operands, TN, BF16 D); bf16 / f16 / tf32 from U[-1,1), i8 from
+    uniform bytes (column-major NN, the reference's cublasGemmEx layout).
+    Returns our launch through the C ABI, the same product through the
+    library (cuBLAS / cuBLASLt via torch) with a view of its output in our
+    D's storage order, the operands and D for the end-to-end copy, and
+    labels."""
     import torch
     import torch.nn.functional as F
     import gplk
     from gplk import operands as O
 
-    n = 8192 if kind == "fp8" else 16384
-    flops = 2.0 * n ** 3
-    xa = O.normal(n, n, 31, dev)
-    if kind == "fp8":
-        qa, sa = O.quantize_fp8(xa)
-        del xa
-        xb = O.normal(n, n, 32, dev)
-        qb, sb = O.quantize_fp8(xb)
-        del xb
-        scale_a = torch.tensor([sa], device=dev)
-        scale_b = torch.tensor([sb], device=dev)
-        D = torch.empty(n, n, dtype=torch.bfloat16, device=dev)  # column-major M x N as (N, M)
-
-        def ours():
-            gplk.gemm_fp8_tn(qa, qb, D, scale_a, scale_b, stream=stream)
-
-        fa, fb = qa.view(torch.float8_e4m3fn), qb.view(torch.float8_e4m3fn)
-
-        def library():
-            return torch._scaled_mm(fa, fb.t(), scale_a=scale_a, scale_b=scale_b, out_dtype=torch.bfloat16)
-
-        lib_name = "cuBLASLt FP8 TN via torch._scaled_mm (per-tensor scales, BF16 out)"
-        inputs = [qa, qb]
-        workload = "FP8 E4M3 TN GEMM M=N=K=8192, N(0,1) operands, per-tensor amax/448 scales, FP32 acc, BF16 out"
-        peak = NOMINAL_TFLOPS["fp8"]
+    c = {"kind": kind, "n": n, "flops": 2.0 * n ** 3, "peak": NOMINAL_TFLOPS[kind]}
+    if kind in ("fp8", "nvfp4"):
+        xa = O.normal(n, n, seed, dev)
+        if kind == "fp8":
+            qa, sa = O.quantize_fp8(xa)
+            del xa
+            xb = O.normal(n, n, seed + 1, dev)
+            qb, sb = O.quantize_fp8(xb)
+            del xb
+            scale_a, scale_b = torch.tensor([sa], device=dev), torch.tensor([sb], device=dev)
+            D = torch.empty(n, n, dtype=torch.bfloat16, device=dev)  # column-major M x N as (N, M)
+            fa, fb = qa.view(torch.float8_e4m3fn), qb.view(torch.float8_e4m3fn)
+            c["ours"] = lambda: gplk.gemm_fp8_tn(qa, qb, D, scale_a, scale_b, stream=stream)
+            c["library"] = lambda: torch._scaled_mm(fa, fb.t(), scale_a=scale_a, scale_b=scale_b,
+                                                    out_dtype=torch.bfloat16)
+            c["library_name"] = "cuBLASLt FP8 TN via torch._scaled_mm (per-tensor scales, BF16 out)"
+            c["inputs"] = [qa, qb]
+            c["dtype"] = "e4m3"
+            c["workload"] = (f"FP8 E4M3 TN GEMM M=N=K={n}, N(0,1) operands, per-tensor amax/448 scales, "
+                             "FP32 acc, BF16 out")
+        else:
+            qa, sfa, ga = O.quantize_nvfp4(xa)
+            del xa
+            xb = O.normal(n, n, seed + 1, dev)
+            qb, sfb, gb = O.quantize_nvfp4(xb)
+            del xb
+            alpha = torch.tensor([ga * gb], device=dev)
+            D = torch.empty(n, n, dtype=torch.bfloat16, device=dev)
+            fa, fb = qa.view(torch.float4_e2m1fn_x2), qb.view(torch.float4_e2m1fn_x2)
+            ssa = sfa.view(torch.float8_e4m3fn).view(n, n // 16)
+            ssb = sfb.view(torch.float8_e4m3fn).view(n // 16, n)
+            gat, gbt = torch.tensor([ga], device=dev), torch.tensor([gb], device=dev)
+            rec = [F.ScalingType.BlockWise1x16, F.ScalingType.TensorWise]
+            sw = [F.SwizzleType.SWIZZLE_32_4_4]
+            c["ours"] = lambda: gplk.gemm_nvfp4_tn(qa, qb, sfa, sfb, D, n, alpha, stream=stream)
+            c["library"] = lambda: F.scaled_mm(fa, fb.t(), [ssa, gat], rec, [ssb, gbt], rec, swizzle_a=sw,
+                                               swizzle_b=sw, output_dtype=torch.bfloat16)
+            c["library_name"] = "cuBLASLt NVFP4 (VEC16 UE4M3 block scales + per-tensor scales) via torch scaled_mm"
+            c["inputs"] = [qa, qb, sfa, sfb]
+            c["dtype"] = "e2m1"
+            c["workload"] = (f"NVFP4 E2M1 TN GEMM M=N=K={n}, N(0,1) operands, UE4M3 per-16 block scales + "
+                             "per-tensor FP32 scale, FP32 acc, BF16 out")
+        c["lib_view"] = lambda out: out  # (M, N) row-major; ours is D.view(N, M).t()
+        c["ours_view"] = lambda: D.view(n, n).t()
     else:
-        qa, sfa, ga = O.quantize_nvfp4(xa)
-        del xa
-        xb = O.normal(n, n, 32, dev)
-        qb, sfb, gb = O.quantize_nvfp4(xb)
-        del xb
-        alpha = torch.tensor([ga * gb], device=dev)
-        D = torch.empty(n, n, dtype=torch.bfloat16, device=dev)
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        if kind == "i8":
+            A = torch.randint(-128, 128, (n, n), dtype=torch.int8, device=dev, generator=g)
+            B = torch.randint(-128, 128, (n, n), dtype=torch.int8, device=dev, generator=g)
+            D = torch.empty(n, n, dtype=torch.int32, device=dev)
+            c["library"] = lambda: torch._int_mm(B, A)
+            c["library_name"] = "cuBLASLt INT8 via torch._int_mm (S32 out)"
+        else:
+            tdt = {"bf16": torch.bfloat16, "f16": torch.float16, "tf32": torch.float32}[kind]
+            A = (torch.rand(n, n, device=dev, generator=g) * 2 - 1).to(tdt)
+            B = (torch.rand(n, n, device=dev, generator=g) * 2 - 1).to(tdt)
+            D = torch.empty(n, n, dtype=tdt, device=dev)
 
-        def ours():
-            gplk.gemm_nvfp4_tn(qa, qb, sfa, sfb, D, n, alpha, stream=stream)
+            def library():
+                if kind == "tf32":
+                    torch.backends.cuda.matmul.allow_tf32 = True
+                return torch.matmul(B, A)
 
-        fa = qa.view(torch.float4_e2m1fn_x2)
-        fb = qb.view(torch.float4_e2m1fn_x2)
-        ssa = sfa.view(torch.float8_e4m3fn).view(n, n // 16)
-        ssb = sfb.view(torch.float8_e4m3fn).view(n // 16, n)
-        gat, gbt = torch.tensor([ga], device=dev), torch.tensor([gb], device=dev)
+            c["library"] = library
+            c["library_name"] = f"cuBLAS {kind.upper()} via torch.matmul" + (" (TF32 allowed)" if kind == "tf32" else "")
+        # Column-major A (M x K) is the row-major (K, M) tensor A; B likewise
+        # (N, K); D stored (N, M) = B-rows x A-columns = torch.matmul(B, A).
+        c["ours"] = lambda: gplk.gemm_nn(kind, A, B, D, n, n, n, stream=stream)
+        c["lib_view"] = lambda out: out
+        c["ours_view"] = lambda: D
+        c["inputs"] = [A, B]
+        c["dtype"], c["workload"] = NN_GEMMS[kind][0], NN_GEMMS[kind][1].replace("8192", str(n))
+        if kind in ("bf16", "f16"):
+            pk = measured_peaks()
+            c["peak"] = pk["bf16_tflops"]
+    c["D"] = D
+    return c
 
-        def library():
-            return F.scaled_mm(fa, fb.t(), [ssa, gat], [F.ScalingType.BlockWise1x16, F.ScalingType.TensorWise],
-                               [ssb, gbt], [F.ScalingType.BlockWise1x16, F.ScalingType.TensorWise],
-                               swizzle_a=[F.SwizzleType.SWIZZLE_32_4_4], swizzle_b=[F.SwizzleType.SWIZZLE_32_4_4],
-                               output_dtype=torch.bfloat16)
 
-        lib_name = "cuBLASLt NVFP4 (VEC16 UE4M3 block scales + per-tensor scales) via torch scaled_mm"
-        inputs = [qa, qb, sfa, sfb]
-        workload = ("NVFP4 E2M1 TN GEMM M=N=K=16384, N(0,1) operands, UE4M3 per-16 block scales + per-tensor "
-                    "FP32 scale, FP32 acc, BF16 out")
-        peak = NOMINAL_TFLOPS["nvfp4"]
+def _case_extras(case: dict, stream, dev, seconds: float, ours_tflops: float, run: dict | None) -> dict:
+    """The library's throughput on the same operands and GPU (sustained for
+    `seconds`, with clocks and power), the relative Frobenius difference of
+    the two outputs, and the GEMM end to end through the C ABI with host
+    operands."""
+    import torch
 
-    run = _sustained(ours, stream, dev, seconds)
-    tflops = flops * run["reps"] / run["s"] / 1e12
-    out = {"metric": f"{kind} GEMM TFLOP/s", "value": round(tflops, 1), "unit": "TFLOP/s", "dtype":
-           "e4m3" if kind == "fp8" else "e2m1", "config": {"workload": workload, "size": n,
-                                                             "l2": "operands larger than L2"},
+    lib = {"impl": case["library_name"]}
+    try:
+        ref = case["library"]()
+        torch.cuda.synchronize(dev)
+        case["ours"]()
+        torch.cuda.synchronize(dev)
+        lib["rel_frob_vs_ours"] = round(_rel_frob(case["ours_view"](), case["lib_view"](ref)), 6)
+        del ref
+        lrun = _sustained(case["library"], stream, dev, seconds)
+        ltf = case["flops"] * lrun["reps"] / lrun["s"] / 1e12
+        lib.update({"value": round(ltf, 1), "unit": "TFLOP/s", "clocks": lrun["clocks"],
+                    "energy": _energy(ltf, lrun), "ours_over_library": round(ours_tflops / ltf, 4)})
+    except Exception as exc:  # the library's kernel for this format may be missing from this torch build
+        lib["unavailable"] = f"{type(exc).__name__}: {str(exc).splitlines()[0][:200]}"
+    out = {"library": lib, "e2e": _gemm_e2e(case["inputs"], case["D"], case["ours"], case["flops"], stream)}
+    if run is not None:
+        out["energy"] = _energy(ours_tflops, run)
+    return out
+
+
+def _sustained_extras(case: dict, stream, dev, seconds: float) -> dict:
+    """For a --workload GEMM line: ours sustained for `seconds` (the short
+    timed region above runs before the power controller settles), then the
+    library the same way, so `ours_over_library` compares like with like."""
+    run = _sustained(case["ours"], stream, dev, seconds)
+    tflops = case["flops"] * run["reps"] / run["s"] / 1e12
+    out = {"sustained": {"value": round(tflops, 1), "unit": "TFLOP/s", "launches": run["reps"],
+                         "seconds": round(run["s"], 3), "clocks": run["clocks"]}}
+    out.update(_case_extras(case, stream, dev, seconds, tflops, run))
+    return out
+
+
+def rung_gemm(kind: str, dev, stream, seconds: float) -> dict:
+    """FP8 E4M3 8192^3 or NVFP4 16384^3 on N(0,1) operands quantised as the
+    rung configuration states, through the C ABI, sustained for `seconds`;
+    the same operands through cuBLASLt on the same GPU beside it; and the
+    GEMM end to end with host operands."""
+    import gplk
+
+    n = 8192 if kind == "fp8" else 16384
+    case = _gemm_case(kind, n, dev, stream)
+    run = _sustained(case["ours"], stream, dev, seconds)
+    tflops = case["flops"] * run["reps"] / run["s"] / 1e12
+    peak = case["peak"]
+    out = {"metric": f"{kind} GEMM TFLOP/s", "value": round(tflops, 1), "unit": "TFLOP/s", "dtype": case["dtype"],
+           "config": {"workload": case["workload"], "size": n, "l2": "operands larger than L2"},
            "launches": run["reps"], "seconds": round(run["s"], 3),
            "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s",
                         "frac": round(tflops / peak, 4), "peak_source": "nominal dense",
                         "traffic": NCU_TRAFFIC.get(kind)},
-           "clocks": run["clocks"], "energy": _energy(tflops, run)}
-    lib_out = {"impl": lib_name}
-    try:
-        ref = library()
-        torch.cuda.synchronize(dev)
-        ours()
-        torch.cuda.synchronize(dev)
-        lib_out["rel_frob_vs_ours"] = round(_rel_frob(D.view(n, n).t(), ref), 6)
-        del ref
-        lrun = _sustained(library, stream, dev, seconds)
-        ltf = flops * lrun["reps"] / lrun["s"] / 1e12
-        lib_out.update({"value": round(ltf, 1), "unit": "TFLOP/s", "clocks": lrun["clocks"],
-                        "energy": _energy(ltf, lrun), "ours_over_library": round(tflops / ltf, 4)})
-    except Exception as exc:  # the library's kernel for this format may be missing from this torch build
-        lib_out["unavailable"] = f"{type(exc).__name__}: {str(exc).splitlines()[0][:200]}"
-    out["library"] = lib_out
-    out["e2e"] = _gemm_e2e(inputs, D, ours, flops, stream)
+           "clocks": run["clocks"]}
+    out.update(_case_extras(case, stream, dev, seconds, tflops, run))
     code, site = gplk.status_read()
     if code != 0:
         raise RuntimeError(f"device status {code} at {site:#x}")
@@ -1050,14 +1275,26 @@ def bench_powervirus(args, dist: Dist) -> dict:
 
     staggered = args.phase == "staggered"
     if dist.world == 1 or staggered:
-        allreduce = None
+        step = None
     elif fab is not None:
-        allreduce = lambda: fab.allreduce_bf16(ar_count, stream=stream)  # noqa: E731
+        step = lambda: fab.allreduce_bf16(ar_count, stream=stream)  # noqa: E731
     else:
-        allreduce = lambda: dist.pg.all_reduce(ar)  # noqa: E731
+        step = lambda: dist.pg.all_reduce(ar)  # noqa: E731
+    # The step is queued behind the burst's last launch (no host round trip)
+    # and timed by CUDA events around it on the burst's stream.
+    fab_ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+
+    def allreduce_timed():
+        fab_ev[0].record(stream)
+        step()
+        fab_ev[1].record(stream)
+
+    allreduce = allreduce_timed if step is not None else None
+    fabric_time = lambda: fab_ev[0].elapsed_time(fab_ev[1]) / 1e3  # noqa: E731
     on_ms, off_ms = args.duty_on_ms, args.duty_off_ms
     offset = rung.phase_offset_s(dist.rank, dist.world, on_ms, off_ms, staggered)
-    rung.run_duty_cycles(max(args.warmup, 3), on_ms, off_ms, launch, sync, allreduce, barrier=dist.barrier)
+    rung.run_duty_cycles(max(args.warmup, 3), on_ms, off_ms, launch, sync, allreduce, barrier=dist.barrier,
+                         fused=True, fabric_time=fabric_time)
     sampler = ClockSampler(dist.local, period_s=0.01)
     sampler.start()
     # Node-level view (rank 0): every GPU of the job sampled from one process
@@ -1074,7 +1311,7 @@ def bench_powervirus(args, dist: Dist) -> dict:
     dist.barrier()
     e0.record(stream)
     log = rung.run_duty_cycles(args.steps, on_ms, off_ms, launch, sync, allreduce, barrier=dist.barrier,
-                               start_offset_s=offset)
+                               start_offset_s=offset, fused=True, fabric_time=fabric_time)
     e1.record(stream)
     torch.cuda.synchronize(dev)
     dist.barrier()
@@ -1130,12 +1367,31 @@ def bench_powervirus(args, dist: Dist) -> dict:
                   "samples": len(watts), "source": "nvml instantaneous power, 10 ms"},
         "node": node,
         "fabric": {"impl": fabric_impl if allreduce else None,
+                   "placement": "queued behind the burst's last launch (no host round trip); CUDA-event timed"
+                   if allreduce else None,
                    "allreduce_bytes": ar_bytes if allreduce else 0, "median_s": round(fabric_s, 6),
                    "busbw_gbs": round(rung.allreduce_busbw_gbs(ar_bytes, fabric_s, dist.world), 1)
                    if allreduce else None},
         "clocks": clocks,
         "gpu_launches": int(sum(log.launches)) + fabric_launches,
     }
+
+
+def pv_cycle(args, dist: Dist) -> dict:
+    """A short in-phase powervirus duty cycle across all ranks (100 ms on /
+    100 ms off, 6 timed cycles after 3 warm-up cycles, each ending in the
+    gplk fabric step, 256 MiB BF16): per-rank power as % of the enforced
+    limit (mean over ranks), node power from the driver's buffered samples,
+    and the fabric step's time inside the cycle."""
+    import copy
+
+    a = copy.copy(args)
+    a.steps, a.warmup = 6, 3
+    a.duty_on_ms, a.duty_off_ms = 100.0, 100.0
+    a.fabric, a.phase = "gplk", "aligned"
+    full = bench_powervirus(a, dist)
+    keep = ("metric", "value", "unit", "ms_per_step", "config", "power", "node", "fabric", "clocks", "gpu_launches")
+    return {k: full[k] for k in keep if k in full}
 
 
 # ------------------------------------------------------------ fabric step alone
@@ -1250,6 +1506,8 @@ def main():
             line["rungs"] = bench_rungs(args, dist)
         if args.workload == "memstream" and dist.world > 1 and not args.no_fabric_check:
             line["fabric"] = fabric_check(dist, args.fabric_mib, steps=10, warmup=3)
+        if args.workload == "memstream" and dist.world > 1 and args.pv_cycle:
+            line["powervirus_cycle"] = pv_cycle(args, dist)
         if dist.rank == 0 and not args.no_cpu and args.workload == "memstream":
             line["cpu_baseline"] = cpu_triad_gbps(args.cpu_seconds)
         dist.barrier()  # the other ranks wait for rank 0's host baseline

@@ -4,9 +4,12 @@
 // both with FP32 accumulation in TMEM and BF16 output, in cuBLASLt's TN
 // convention (A and B K-major, D column-major M x N).
 //
-// One persistent CTA per SM walks output tiles of 128 x 256 in a grouped
+// One persistent CTA per SM walks output tiles of 128 x BN in a grouped
 // (L2-friendly) order, launched with programmatic stream serialisation (its
-// set-up overlaps the previous GEMM on the stream). Warp roles:
+// set-up overlaps the previous GEMM on the stream). BN is 256 for NVFP4 and
+// for FP8 problems with a single 128-row block; small FP8 problems take
+// BN = 128 or 64 so their tiles cover more of the 148 SMs (1024^3 has 16
+// CTA-pair tiles of 256 x 256 but 128 tiles of 128 x 64). Warp roles:
 //   warp 0      TMA producer: 2-D tiled loads of A (128 rows) and B (256
 //               rows), 128 bytes of K per stage with 128-byte swizzle, into a
 //               STAGES-deep shared-memory ring; NVFP4 adds 1-D bulk copies of
@@ -32,21 +35,23 @@ namespace gplk {
 namespace gemm_tc {
 
 constexpr int BM = 128;
-constexpr int BN = 256;
 constexpr int BK_BYTES = 128;  // one 128-byte swizzle row of K per stage
 constexpr int A_STAGE = BM * BK_BYTES;   // 16 KiB
-constexpr int B_STAGE = BN * BK_BYTES;   // 32 KiB
 constexpr int SFA_STAGE = 4 * 512;       // 4 K-blocks of 128 rows x 4 scales
 constexpr int SFB_STAGE = 8 * 512;       // 2 row-halves x 4 K-blocks
 constexpr int kThreads = 192;
 constexpr int kGroupM = 8;               // tile raster group along M
 
-template <bool NVF4>
+template <bool NVF4, int BN = 256>
 struct Traits {
-    static constexpr int kStages = 4;
-    static constexpr int kStageBytes = A_STAGE + B_STAGE + (NVF4 ? SFA_STAGE + SFB_STAGE : 0);
+    static_assert(BN == 256 || (!NVF4 && (BN == 128 || BN == 64)), "tile width");
+    static constexpr int kBN = BN;
+    static constexpr int kBStage = BN * BK_BYTES;  // 32 / 16 / 8 KiB
+    // Narrower tiles have smaller stages: a deeper ring in the same memory.
+    static constexpr int kStages = BN == 256 ? 4 : 6;
+    static constexpr int kStageBytes = A_STAGE + kBStage + (NVF4 ? SFA_STAGE + SFB_STAGE : 0);
     static constexpr int kAccBufs = NVF4 ? 1 : 2;
-    static constexpr uint32_t kTmemCols = 512;
+    static constexpr uint32_t kTmemCols = NVF4 ? 512u : (uint32_t)(2 * BN);
     // TMEM column map. Accumulators first; NVFP4 scale factors after them,
     // one 48-column slot per stage (16 for A, 32 for B).
     static constexpr uint32_t kSfCol0 = 256;
@@ -54,12 +59,12 @@ struct Traits {
     static_assert(!NVF4 || kSfCol0 + kStages * kSfColsPerStage <= kTmemCols, "TMEM budget");
 };
 
-template <bool NVF4>
+template <bool NVF4, int BN = 256>
 struct __align__(1024) Smem {
-    uint8_t stage[Traits<NVF4>::kStages][Traits<NVF4>::kStageBytes];
+    uint8_t stage[Traits<NVF4, BN>::kStages][Traits<NVF4, BN>::kStageBytes];
     uint8_t out_stage[NVF4 ? 128 * 32 * 2 : 16];  // NVFP4 epilogue staging: 128 rows x 32 BF16
-    uint64_t full[Traits<NVF4>::kStages];
-    uint64_t empty[Traits<NVF4>::kStages];
+    uint64_t full[Traits<NVF4, BN>::kStages];
+    uint64_t empty[Traits<NVF4, BN>::kStages];
     uint64_t acc_full[2];
     uint64_t acc_empty[2];
     uint64_t drain;
@@ -93,14 +98,15 @@ __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int
     nt = r / gsize;
 }
 
-template <bool NVF4>
+template <bool NVF4, int BN = 256>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmD, const Params p) {
-    using TR = Traits<NVF4>;
+    using TR = Traits<NVF4, BN>;
     constexpr int S = TR::kStages;
+    constexpr int B_STAGE = TR::kBStage;
     extern __shared__ uint8_t smem_raw[];
-    Smem<NVF4>& sm = *reinterpret_cast<Smem<NVF4>*>(
+    Smem<NVF4, BN>& sm = *reinterpret_cast<Smem<NVF4, BN>*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
 
     const uint32_t warp = warp_id_uniform();
@@ -207,7 +213,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d_tmem = tmem + (uint32_t)acc * 256u;
+                const uint32_t d_tmem = tmem + (uint32_t)acc * (uint32_t)BN;
                 for (int kb = 0; kb < p.k_stages; ++kb) {
                     if (!mbar_wait(&sm.full[stage], phase, &sm.abort, 0x0212)) {
                         ok = false;
@@ -279,7 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const int m = mt * BM + row_in_tile;
             const int n_base = nt * BN;
-            const uint32_t t_addr = tmem + ((quarter * 32u) << 16) + (uint32_t)acc * 256u;
+            const uint32_t t_addr = tmem + ((quarter * 32u) << 16) + (uint32_t)acc * (uint32_t)BN;
             uint16_t* drow = p.D + m;  // column-major: D[m + n * M]
             const size_t ldd = (size_t)p.M;
             if constexpr (NVF4) {
@@ -330,7 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             } else {
 #pragma unroll 1
-                for (int c = 0; c < 8; ++c) {
+                for (int c = 0; c < BN / 32; ++c) {
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(t_addr + 32u * c, r);
                     tmem_ld_wait();
@@ -366,25 +372,25 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 
-template <bool NVF4>
+template <bool NVF4, int BN>
 static int smem_bytes() {
-    return (int)sizeof(Smem<NVF4>) + 1024;
+    return (int)sizeof(Smem<NVF4, BN>) + 1024;
 }
 
-template <bool NVF4>
+template <bool NVF4, int BN = 256>
 static int launch(const uint8_t* A, const uint8_t* B, const uint8_t* SFA, const uint8_t* SFB,
                   uint16_t* D, int M, int N, int K, const float* sa, const float* sb,
                   cudaStream_t stream) {
     DeviceInfo d;
     int st = require_sm100(&d);
     if (st != GPLK_STATUS_OK) return st;
-    const int smem = smem_bytes<NVF4>();
+    const int smem = smem_bytes<NVF4, BN>();
     if (smem > d.max_smem_optin) return GPLK_STATUS_UNSUPPORTED;
     static thread_local uint64_t configured = 0;  // bit per device
     int dev = 0;
     cudaGetDevice(&dev);
     if (!(configured & (1ull << dev))) {
-        if (cudaFuncSetAttribute(gemm_tc_kernel<NVF4>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        if (cudaFuncSetAttribute(gemm_tc_kernel<NVF4, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
             cudaSuccess)
             return GPLK_STATUS_LAUNCH_FAIL;
         configured |= 1ull << dev;
@@ -424,8 +430,35 @@ static int launch(const uint8_t* A, const uint8_t* B, const uint8_t* SFA, const 
     }
     const int tiles = p.m_tiles * p.n_tiles;
     const int grid = tiles < d.sm_count ? tiles : d.sm_count;
-    return launch_status(launch_pdl(gemm_tc_kernel<NVF4>, dim3(grid), dim3(kThreads), (size_t)smem, stream, tmA,
-                                    tmB, tmD, p));
+    return launch_status(launch_pdl(gemm_tc_kernel<NVF4, BN>, dim3(grid), dim3(kThreads), (size_t)smem, stream,
+                                    tmA, tmB, tmD, p));
+}
+
+// FP8 tile shape: the CTA-pair kernel's 256 x 256 tiles, or single-CTA
+// 128 x BN tiles with BN = 256 / 128 / 64. Narrower tiles are considered
+// only when the widest choice fills less than nine tenths of one wave of
+// the SMs (small problems); each candidate is then scored by the slowest
+// SM's share of the output (waves x output elements per SM and tile), with
+// narrower tiles weighted for their lower operand reuse, and ties go to the
+// wider tile. Returns 0 for the pair kernel, else BN.
+static int fp8_tile(int M, int N, int sm_count) {
+    const bool pair = M > 128;
+    const long slots = pair ? sm_count / 2 : sm_count;
+    const long wide_tiles = pair ? (long)((M + 255) / 256) * ((N + 255) / 256) : (long)((N + 255) / 256);
+    int choice = pair ? 0 : 256;
+    if (10 * wide_tiles >= 9 * slots) return choice;
+    double best = (double)((wide_tiles + slots - 1) / slots) * (128.0 * 256.0);
+    const int widths[2] = {128, 64};
+    const double weight[2] = {1.1, 1.25};
+    for (int i = 0; i < 2; ++i) {
+        const long tiles = (long)((M + 127) / 128) * ((N + widths[i] - 1) / widths[i]);
+        const double cost = (double)((tiles + sm_count - 1) / sm_count) * (128.0 * widths[i]) * weight[i];
+        if (cost < best) {
+            best = cost;
+            choice = widths[i];
+        }
+    }
+    return choice;
 }
 
 }  // namespace gemm_tc
@@ -442,8 +475,15 @@ extern "C" int gplk_gemm_fp8_tn(const uint8_t* A, const uint8_t* B, uint16_t* D,
     // Problems with at least two 128-row blocks run on CTA pairs (256 x 256
     // tiles, cta_group::2, gplk_gemm_pair.cu); a single row block runs on
     // single CTAs (128 x 256 tiles).
-    if (M > 128) return pair::launch<pair::CfgFP8>(A, B, D, M, N, K, stream, scale_a, scale_b);
-    return gemm_tc::launch<false>(A, B, nullptr, nullptr, D, M, N, K, scale_a, scale_b, stream);
+    DeviceInfo d;
+    const int st = current_device_info(&d);
+    if (st != GPLK_STATUS_OK) return st;
+    switch (gemm_tc::fp8_tile(M, N, d.sm_count)) {
+        case 0: return pair::launch<pair::CfgFP8>(A, B, D, M, N, K, stream, scale_a, scale_b);
+        case 128: return gemm_tc::launch<false, 128>(A, B, nullptr, nullptr, D, M, N, K, scale_a, scale_b, stream);
+        case 64: return gemm_tc::launch<false, 64>(A, B, nullptr, nullptr, D, M, N, K, scale_a, scale_b, stream);
+        default: return gemm_tc::launch<false, 256>(A, B, nullptr, nullptr, D, M, N, K, scale_a, scale_b, stream);
+    }
 }
 
 extern "C" size_t gplk_nvfp4_sf_bytes(int rows, int k) {

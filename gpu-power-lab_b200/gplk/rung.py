@@ -35,7 +35,8 @@ class CycleLog:
 def run_duty_cycles(cycles: int, on_ms: float, off_ms: float, launch: Callable[[], None], sync: Callable[[], None],
                     allreduce: Callable[[], None] | None, barrier: Callable[[], None] | None = None,
                     sync_every: int = 8, clock: Callable[[], float] = time.time,
-                    sleep: Callable[[float], None] = time.sleep, start_offset_s: float = 0.0) -> CycleLog:
+                    sleep: Callable[[float], None] = time.sleep, start_offset_s: float = 0.0,
+                    fused: bool = False, fabric_time: Callable[[], float] | None = None) -> CycleLog:
     """Run `cycles` duty cycles: launch kernels back to back for on_ms
     (syncing every `sync_every` launches, as the reference's batches do),
     then the fabric allreduce, then sleep off_ms. `barrier` (optional) aligns
@@ -43,7 +44,15 @@ def run_duty_cycles(cycles: int, on_ms: float, off_ms: float, launch: Callable[[
     `start_offset_s` then delays this rank's first cycle, which staggers the
     ranks' phases (rank r of N at r x period / N spreads them evenly). With a
     fabric step every cycle the collective re-aligns the ranks, so staggering
-    is meaningful without one (allreduce None)."""
+    is meaningful without one (allreduce None).
+
+    fused: the burst's last launch is not waited for; the allreduce is
+    queued right behind it on the same stream, so the device goes from the
+    burst to the fabric step with no host round trip in between (the launch
+    reaching the end of the burst is predicted from the previous launch's
+    duration). fabric_time() then gives the step's own time (e.g. from CUDA
+    events the allreduce recorded), read after the sync; without it the host
+    clock brackets the step."""
     log = CycleLog()
     if barrier is not None:
         barrier()
@@ -53,12 +62,20 @@ def run_duty_cycles(cycles: int, on_ms: float, off_ms: float, launch: Callable[[
         t0 = clock()
         log.burst_start.append(t0)
         n = 0
-        while (clock() - t0) * 1e3 < on_ms:
+        last_s = 0.0  # duration of the previous launch (fused mode)
+        while (clock() - t0) * 1e3 < on_ms or (fused and allreduce is not None):
+            tl = clock()
             launch()
             n += 1
-            if n % sync_every == 0:
+            if fused and allreduce is not None:
+                if (tl - t0 + last_s) * 1e3 >= on_ms:
+                    break  # this launch ends the burst: the fabric step goes right behind it
                 sync()
-        sync()
+                last_s = clock() - tl
+            elif n % sync_every == 0:
+                sync()
+        if not (fused and allreduce is not None):
+            sync()
         t1 = clock()
         log.burst_end.append(t1)
         log.launches.append(n)
@@ -67,7 +84,7 @@ def run_duty_cycles(cycles: int, on_ms: float, off_ms: float, launch: Callable[[
             sync()
         t2 = clock()
         log.fabric_end.append(t2)
-        log.fabric_s.append(t2 - t1)
+        log.fabric_s.append(fabric_time() if (allreduce is not None and fabric_time is not None) else t2 - t1)
         if off_ms > 0:
             sleep(off_ms / 1e3)
         log.cycle_end.append(clock())

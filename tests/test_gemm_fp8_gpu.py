@@ -1,5 +1,6 @@
 """FP8 E4M3 TN GEMM (tcgen05) against the double-accumulated oracle on the
-same quantised operands, and against the reference's own cuBLASLt wrapper
+same quantised operands (shapes that take every tile choice: CTA-pair
+256 x 256, single-CTA 128 x 256 / 128 x 128 / 128 x 64), and against the reference's own cuBLASLt wrapper
 (runner/src/gemm_lt.cu, compiled into oracle/_ref) at the 8192^3 rung.
 Bar: relative Frobenius error <= 1e-2 (BF16 output)."""
 from __future__ import annotations
@@ -42,7 +43,9 @@ def _run(gplk, qa, sa, qb, sb, cuda):
 
 @pytest.mark.parametrize("mnk", [(128, 256, 128), (256, 256, 256), (512, 512, 1024), (1024, 768, 512), (300, 520, 256), (136, 264, 384),
                                  (200, 300, 512), (129, 257, 144), (1, 1, 16), (640, 1280, 2048),
-                                 (4352, 264, 128)])  # 17 pair-tile rows: a second, one-row raster group
+                                 (4352, 264, 128),   # 1-CTA 128 x 128 tiles (too few pair tiles for one wave)
+                                 (4352, 2304, 128),  # pair tiles: 17 rows, a second, one-row raster group
+                                 (1536, 1536, 512), (1000, 1000, 1008)])  # 1-CTA 128 x 128 / 128 x 64 tiles
 def test_fp8_full_vs_oracle(mnk, gplk, oracle, cuda):
     M, N, K = mnk
     qa, sa, qb, sb = _operands(oracle, M, N, K, seed=M * 7 + N)

@@ -127,3 +127,37 @@ def test_phase_offsets():
 
     assert rung.phase_offset_s(3, 8, 100, 100, staggered=False) == 0.0
     assert [rung.phase_offset_s(r, 4, 100, 100, True) for r in range(4)] == pytest.approx([0, 0.05, 0.1, 0.15])
+
+
+def test_fused_burst_end_queues_step_behind_last_launch():
+    """Fused mode on a fake device: the launch that reaches the end of the
+    burst is not waited for, the allreduce follows it directly, and the
+    fabric time comes from the supplied timer."""
+    from gplk import rung
+
+    t = [0.0]
+    events = []
+
+    def clock():
+        return t[0]
+
+    def launch():
+        events.append("launch")
+        t[0] += 0.004  # each launch takes 4 ms of host time to enqueue and run
+
+    def sync():
+        events.append("sync")
+
+    def allreduce():
+        events.append("allreduce")
+
+    log = rung.run_duty_cycles(cycles=2, on_ms=20, off_ms=0, launch=launch, sync=sync, allreduce=allreduce,
+                               clock=clock, sleep=lambda s: None, fused=True, fabric_time=lambda: 0.5e-3)
+    for c in range(2):
+        # within one cycle: launches separated by syncs, then launch, allreduce, sync
+        seq = events[: events.index("allreduce") + 2]
+        events[: len(seq)] = []
+        assert seq[-3:] == ["launch", "allreduce", "sync"], seq
+        assert seq.count("launch") == log.launches[c]
+    assert log.fabric_s == [0.5e-3, 0.5e-3]
+    assert all(n >= 4 for n in log.launches)
