@@ -529,203 +529,6 @@ def bench_gemm(args, dist: Dist) -> dict:
     torch.cuda.synchronize()
     sampler = ClockSampler(dist.local)
     dist.barrier()
-    torch.cuda.synchronize()
-    sampler.start()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    dist.barrier()
-    sampler.stop()
-    ms = e0.elapsed_time(e1)
-    ms_max = dist.max(ms)
-    code, site = gplk.status_read()
-    if code != 0:
-        raise RuntimeError(f"device status {code} at {site:#x}")
-
-    per_launch_s = ms / 1e3 / args.steps
-    achieved = nbytes / per_launch_s / 1e9
-    peaks = measured_peaks()
-    value = dist.world * nbytes * args.steps / (ms_max / 1e3) / 1e9
-
-    e2e = None
-    if not args.no_e2e:
-        e2e = memstream_e2e(a, b, c, stream, bulk, dist, steps=3)
-    if n != TRIAD_N:
-        workload = f"memstream STREAM triad a = b + 3.0*c, FP32, 3 x {n} elements (profiling case)"
-    else:
-        workload = "memstream STREAM triad a = b + 3.0*c, FP32, 3 x 2^30 elements (4 GiB each)"
-
-    traffic = NCU_TRAFFIC["memstream_bulk" if bulk else "memstream_vec4"] if n == TRIAD_N else None
-    out = {
-        "metric": "memstream triad GB/s",
-        "value": round(value, 2),
-        "unit": "GB/s",
-        "n_gpus": dist.world,
-        "steps": args.steps,
-        "warmup": max(args.warmup, 3),
-        "ms_per_step": round(ms_max / args.steps, 4),
-        "higher_is_better": True,
-        "scaling": "weak",
-        "vs_baseline": None,
-        "dtype": "f32",
-        "data": "synthetic: b, c ~ U[0,1) from torch's seeded generator, s = 3.0",
-        "config": {"workload": workload,
-                   "elements": n, "bytes_per_step_per_gpu": nbytes,
-                   "kernel": "triad_bulk" if bulk else "triad_vec4",
-                   "l2": "inputs (12 GiB per step) larger than the 126 MB L2; no flush",
-                   "parallelism": f"replicas x{dist.world} (the workload does not shard)"},
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
-                     "peak_source": f"{peaks['_source']} hbm_gbs (burst copy)",
-                     "algorithmic_bytes_per_launch": nbytes},
-        "clocks": sampler.summary(),
-        "gpu_launches": args.steps,
-    }
-    if e2e:
-        out["e2e"] = e2e
-    return out
-
-
-def memstream_e2e(a, b, c, stream, bulk, dist: Dist, steps: int, chunk: int = 1 << 24) -> dict:
-    """The same triad through the C ABI with host buffers: every step copies
-    b and c from pinned host memory, runs the triad and reads a back, all of
-    it. The arrays move in chunks of `chunk` elements on three streams
-    (copy in, triad, copy out), so the host-to-device copies of later chunks
-    overlap the device-to-host copies of earlier ones: PCIe carries both
-    directions at once. Events keep every chunk's order: a chunk is
-    overwritten only after the previous step's triad read it, and a is
-    rewritten only after the previous step copied it out."""
-    import torch
-    import gplk
-
-    n = b.numel()
-    hb = torch.empty(n, dtype=torch.float32, pin_memory=True)
-    hc = torch.empty(n, dtype=torch.float32, pin_memory=True)
-    ha = torch.empty(n, dtype=torch.float32, pin_memory=True)
-    hb.copy_(b, non_blocking=False)
-    hc.copy_(c, non_blocking=False)
-    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
-    bounds = [(k, min(k + chunk, n)) for k in range(0, n, chunk)]
-    ev_in = [torch.cuda.Event() for _ in bounds]
-    ev_tr = [torch.cuda.Event() for _ in bounds]
-    ev_out = [torch.cuda.Event() for _ in bounds]
-    first = [True]
-
-    def step():
-        for i, (lo, hi) in enumerate(bounds):
-            if not first[0]:
-                s_in.wait_event(ev_tr[i])  # the previous step's triad has read b, c here
-            with torch.cuda.stream(s_in):
-                b[lo:hi].copy_(hb[lo:hi], non_blocking=True)
-                c[lo:hi].copy_(hc[lo:hi], non_blocking=True)
-                ev_in[i].record(s_in)
-            stream.wait_event(ev_in[i])
-            if not first[0]:
-                stream.wait_event(ev_out[i])  # the previous step has copied a out of here
-            gplk.triad(a[lo:hi], b[lo:hi], c[lo:hi], TRIAD_S, stream=stream, bulk=bulk)
-            ev_tr[i].record(stream)
-            s_out.wait_event(ev_tr[i])
-            with torch.cuda.stream(s_out):
-                ha[lo:hi].copy_(a[lo:hi], non_blocking=True)
-                ev_out[i].record(s_out)
-        first[0] = False
-
-    step()
-    torch.cuda.synchronize()
-    dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(s_in)
-    for _ in range(steps):
-        step()
-    s_out.wait_event(ev_tr[-1])
-    e1.record(s_out)  # after the last copy out, which follows every chunk's triad
-    torch.cuda.synchronize()
-    ms = dist.max(e0.elapsed_time(e1))
-    value = dist.world * 12 * n * steps / (ms / 1e3) / 1e9
-    return {"value": round(value, 2), "unit": "GB/s", "h2d_bytes_per_step": 8 * n,
-            "d2h_bytes_per_step": 4 * n, "steps": steps,
-            "note": f"pinned host b, c -> device, triad, device a -> pinned host, per step, in "
-                    f"{len(bounds)} chunks on three streams (copy in / triad / copy out overlap)"}
-
-
-# ------------------------------------------------------------ GEMM rungs
-
-def bench_gemm(args, dist: Dist) -> dict:
-    import torch
-    import gplk
-
-    dev = torch.device("cuda", dist.local)
-    torch.cuda.set_device(dev)
-    gplk.lib()
-    g = torch.Generator(device=dev)
-    g.manual_seed(7 + dist.rank)
-    stream = torch.cuda.current_stream(dev)
-    w = args.workload
-    if w == "sgemm":
-        n = args.sgemm_n
-        A = torch.rand(n, n, device=dev, generator=g) * 2 - 1
-        B = torch.rand(n, n, device=dev, generator=g) * 2 - 1
-        C = torch.empty(n, n, device=dev)
-        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-
-        def step():
-            flush.zero_()  # 256 MiB write: evicts the 12 MiB working set from L2
-            gplk.sgemm(A, B, C, stream=stream)
-
-        dtype, workload = "f32", f"FP32 SGEMM C = A*B row-major, M=N=K={n}, U[-1,1)"
-        launches_per_step = 2
-    elif w in NN_GEMMS:
-        n = args.gemm_n or 8192
-        if w == "i8":
-            A = torch.randint(-128, 128, (n, n), dtype=torch.int8, device=dev, generator=g)
-            B = torch.randint(-128, 128, (n, n), dtype=torch.int8, device=dev, generator=g)
-            D = torch.empty(n, n, dtype=torch.int32, device=dev)
-        else:
-            tdt = {"bf16": torch.bfloat16, "f16": torch.float16, "tf32": torch.float32}[w]
-            A = (torch.rand(n, n, device=dev, generator=g) * 2 - 1).to(tdt)
-            B = (torch.rand(n, n, device=dev, generator=g) * 2 - 1).to(tdt)
-            D = torch.empty(n, n, dtype=tdt, device=dev)
-
-        def step():
-            gplk.gemm_nn(w, A, B, D, n, n, n, stream=stream)
-
-        dtype, workload = NN_GEMMS[w]
-        launches_per_step = 1
-    else:
-        n = args.gemm_n or (8192 if w == "fp8" else 16384)
-        if w == "fp8":
-            A = (torch.randn(n, n, device=dev, generator=g) * 32).clamp(-448, 448).to(torch.float8_e4m3fn).view(torch.uint8)
-            B = (torch.randn(n, n, device=dev, generator=g) * 32).clamp(-448, 448).to(torch.float8_e4m3fn).view(torch.uint8)
-            D = torch.empty(n, n, dtype=torch.bfloat16, device=dev)
-            s = torch.ones(1, device=dev)
-
-            def step():
-                gplk.gemm_fp8_tn(A, B, D, s, s, stream=stream)
-
-            dtype, workload = "e4m3", "FP8 E4M3 TN GEMM M=N=K=8192, per-tensor scales, BF16 out"
-        else:
-            A = torch.randint(0, 256, (n, n // 2), dtype=torch.uint8, device=dev, generator=g)
-            B = torch.randint(0, 256, (n, n // 2), dtype=torch.uint8, device=dev, generator=g)
-            sfb = gplk.nvfp4_sf_bytes(n, n)
-            SFA = torch.full((sfb,), 0x38, dtype=torch.uint8, device=dev)
-            SFB = torch.full((sfb,), 0x38, dtype=torch.uint8, device=dev)
-            D = torch.empty(n, n, dtype=torch.bfloat16, device=dev)
-            al = torch.ones(1, device=dev)
-
-            def step():
-                gplk.gemm_nvfp4_tn(A, B, SFA, SFB, D, n, al, stream=stream)
-
-            dtype, workload = "e2m1", "NVFP4 E2M1 TN GEMM M=N=K=16384, UE4M3 per-16 scales, BF16 out"
-        launches_per_step = 1
-
-    for _ in range(max(args.warmup, 3)):
-        step()
-    torch.cuda.synchronize()
-    sampler = ClockSampler(dist.local)
-    dist.barrier()
     sampler.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
