@@ -625,10 +625,13 @@ def fma_peak_tflops(dev, stream, inner: int = 10000, launches: int = 60) -> dict
 
 # ------------------------------------------------------------ the metric's other rungs (N = 1 line)
 
-def _sustained(fn, stream, dev, seconds: float, skip_s: float = 0.3) -> dict:
-    """Run fn back to back for about `seconds` (count fixed from a short
-    timing first), CUDA events around the whole run on `stream`, NVML
-    clocks and power sampled meanwhile."""
+def _sustained(fn, stream, dev, seconds: float, skip_s: float = 0.3, graph: bool = True) -> dict:
+    """Run fn back to back for about `seconds`, CUDA events around the whole
+    run on `stream`, NVML clocks and power sampled meanwhile. With `graph`,
+    the launches are captured into a CUDA graph of about 2 ms of work and
+    the graph is replayed, so host launch overhead (a Python call per
+    launch) does not limit small problems; both arms of a comparison are
+    timed the same way. A capture that fails falls back to direct launches."""
     import torch
 
     for _ in range(3):
@@ -640,17 +643,37 @@ def _sustained(fn, stream, dev, seconds: float, skip_s: float = 0.3) -> dict:
         fn()
     e1.record(stream)
     torch.cuda.synchronize(dev)
-    reps = max(5, int(seconds / max(e0.elapsed_time(e1) / 5e3, 1e-6)))
+    per = max(e0.elapsed_time(e1) / 5e3, 1e-6)
+    launch = fn
+    per_call, how = 1, "direct launches"
+    if graph:
+        k = max(1, min(64, int(2e-3 / per)))
+        try:
+            g = torch.cuda.CUDAGraph()
+            side = torch.cuda.Stream(device=dev)
+            side.wait_stream(stream)
+            with torch.cuda.stream(side), torch.cuda.graph(g, stream=side):
+                for _ in range(k):
+                    fn()
+            torch.cuda.synchronize(dev)
+            g.replay()
+            torch.cuda.synchronize(dev)
+            launch, per_call, how = g.replay, k, f"CUDA graph of {k} launches, replayed"
+        except Exception as exc:  # capture refused: time direct launches
+            torch.cuda.synchronize(dev)
+            how = f"direct launches (graph capture failed: {type(exc).__name__})"
+    calls = max(2, int(seconds / (per * per_call)))
     sampler = ClockSampler(dev.index if dev.index is not None else 0, period_s=0.02)
     sampler.start()
     e0.record(stream)
-    for _ in range(reps):
-        fn()
+    with torch.cuda.stream(stream):
+        for _ in range(calls):
+            launch()
     e1.record(stream)
     torch.cuda.synchronize(dev)
     sampler.stop()
-    return {"reps": reps, "s": e0.elapsed_time(e1) / 1e3, "clocks": sampler.summary(),
-            "power": sampler.power_stats(skip_s)}
+    return {"reps": calls * per_call, "s": e0.elapsed_time(e1) / 1e3, "clocks": sampler.summary(),
+            "power": sampler.power_stats(skip_s), "timing": how}
 
 
 def _energy(tflops: float, run: dict) -> dict:
@@ -725,7 +748,7 @@ def _gemm_case(kind: str, n: int, dev, stream, seed: int = 31) -> dict:
             scale_a, scale_b = torch.tensor([sa], device=dev), torch.tensor([sb], device=dev)
             D = torch.empty(n, n, dtype=torch.bfloat16, device=dev)  # column-major M x N as (N, M)
             fa, fb = qa.view(torch.float8_e4m3fn), qb.view(torch.float8_e4m3fn)
-            c["ours"] = lambda: gplk.gemm_fp8_tn(qa, qb, D, scale_a, scale_b, stream=stream)
+            c["ours"] = lambda: gplk.gemm_fp8_tn(qa, qb, D, scale_a, scale_b)
             c["library"] = lambda: torch._scaled_mm(fa, fb.t(), scale_a=scale_a, scale_b=scale_b,
                                                     out_dtype=torch.bfloat16)
             c["library_name"] = "cuBLASLt FP8 TN via torch._scaled_mm (per-tensor scales, BF16 out)"
@@ -747,7 +770,7 @@ def _gemm_case(kind: str, n: int, dev, stream, seed: int = 31) -> dict:
             gat, gbt = torch.tensor([ga], device=dev), torch.tensor([gb], device=dev)
             rec = [F.ScalingType.BlockWise1x16, F.ScalingType.TensorWise]
             sw = [F.SwizzleType.SWIZZLE_32_4_4]
-            c["ours"] = lambda: gplk.gemm_nvfp4_tn(qa, qb, sfa, sfb, D, n, alpha, stream=stream)
+            c["ours"] = lambda: gplk.gemm_nvfp4_tn(qa, qb, sfa, sfb, D, n, alpha)
             c["library"] = lambda: F.scaled_mm(fa, fb.t(), [ssa, gat], rec, [ssb, gbt], rec, swizzle_a=sw,
                                                swizzle_b=sw, output_dtype=torch.bfloat16)
             c["library_name"] = "cuBLASLt NVFP4 (VEC16 UE4M3 block scales + per-tensor scales) via torch scaled_mm"
@@ -781,7 +804,7 @@ def _gemm_case(kind: str, n: int, dev, stream, seed: int = 31) -> dict:
             c["library_name"] = f"cuBLAS {kind.upper()} via torch.matmul" + (" (TF32 allowed)" if kind == "tf32" else "")
         # Column-major A (M x K) is the row-major (K, M) tensor A; B likewise
         # (N, K); D stored (N, M) = B-rows x A-columns = torch.matmul(B, A).
-        c["ours"] = lambda: gplk.gemm_nn(kind, A, B, D, n, n, n, stream=stream)
+        c["ours"] = lambda: gplk.gemm_nn(kind, A, B, D, n, n, n)
         c["lib_view"] = lambda out: out
         c["ours_view"] = lambda: D
         c["inputs"] = [A, B]
@@ -810,7 +833,7 @@ def _case_extras(case: dict, stream, dev, seconds: float, ours_tflops: float, ru
         del ref
         lrun = _sustained(case["library"], stream, dev, seconds)
         ltf = case["flops"] * lrun["reps"] / lrun["s"] / 1e12
-        lib.update({"value": round(ltf, 1), "unit": "TFLOP/s", "clocks": lrun["clocks"],
+        lib.update({"value": round(ltf, 1), "unit": "TFLOP/s", "timing": lrun["timing"], "clocks": lrun["clocks"],
                     "energy": _energy(ltf, lrun), "ours_over_library": round(ours_tflops / ltf, 4)})
     except Exception as exc:  # the library's kernel for this format may be missing from this torch build
         lib["unavailable"] = f"{type(exc).__name__}: {str(exc).splitlines()[0][:200]}"
@@ -827,7 +850,7 @@ def _sustained_extras(case: dict, stream, dev, seconds: float) -> dict:
     run = _sustained(case["ours"], stream, dev, seconds)
     tflops = case["flops"] * run["reps"] / run["s"] / 1e12
     out = {"sustained": {"value": round(tflops, 1), "unit": "TFLOP/s", "launches": run["reps"],
-                         "seconds": round(run["s"], 3), "clocks": run["clocks"]}}
+                         "seconds": round(run["s"], 3), "timing": run["timing"], "clocks": run["clocks"]}}
     out.update(_case_extras(case, stream, dev, seconds, tflops, run))
     return out
 
@@ -846,7 +869,7 @@ def rung_gemm(kind: str, dev, stream, seconds: float) -> dict:
     peak = case["peak"]
     out = {"metric": f"{kind} GEMM TFLOP/s", "value": round(tflops, 1), "unit": "TFLOP/s", "dtype": case["dtype"],
            "config": {"workload": case["workload"], "size": n, "l2": "operands larger than L2"},
-           "launches": run["reps"], "seconds": round(run["s"], 3),
+           "launches": run["reps"], "seconds": round(run["s"], 3), "timing": run["timing"],
            "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s",
                         "frac": round(tflops / peak, 4), "peak_source": "nominal dense",
                         "traffic": NCU_TRAFFIC.get(kind)},
@@ -881,7 +904,8 @@ def rung_power(dev, stream, seconds: float, mix=(4, 1, 2), budget_us: float = 10
     time.sleep(0.5)
     idle.stop()
     idle_w = idle.power_stats().get("avg_w")
-    run = _sustained(lambda: gplk.powervirus_launch(cfg, stream=stream), stream, dev, seconds, skip_s=0.5)
+    run = _sustained(lambda: gplk.powervirus_launch(cfg, stream=stream), stream, dev, seconds, skip_s=0.5,
+                     graph=False)  # 1 ms launches: no launch overhead to hide
     limit = run["power"].get("limit_w") or 1000.0
     lvl = run["power"].get("avg_w") or 0.0
     out = {"metric": "powervirus sustained power % of enforced limit", "value": round(100.0 * lvl / limit, 2),
@@ -903,7 +927,7 @@ def rung_power(dev, stream, seconds: float, mix=(4, 1, 2), budget_us: float = 10
         b = torch.full((n, n), 0x38, dtype=torch.uint8, device=dev).view(torch.float8_e4m3fn)
         one = torch.ones(1, device=dev)
         lrun = _sustained(lambda: torch._scaled_mm(a, b.t(), scale_a=one, scale_b=one, out_dtype=torch.bfloat16),
-                          stream, dev, seconds, skip_s=0.5)
+                          stream, dev, seconds, skip_s=0.5, graph=False)
         llvl = lrun["power"].get("avg_w") or 0.0
         lib.update({"value": round(100.0 * llvl / limit, 2), "unit": "%", "power": lrun["power"],
                     "clocks": lrun["clocks"]})

@@ -17,8 +17,10 @@
 //   warp 1      owns TMEM; one thread issues the MMAs (4 per stage: K = 32
 //               FP8 or 64 FP4 elements per instruction) and, for NVFP4,
 //               the shared->TMEM copies of the scale factors first.
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator, scale, BF16, global
-//               stores. Warp w reads TMEM lanes 32*(w%4)..+31 (= tile rows).
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator, scale, BF16, staged
+//               in shared memory and written by TMA stores (plain stores when
+//               D's rows are not 16-byte multiples). Warp w reads TMEM lanes
+//               32*(w%4)..+31 (= tile rows).
 // FP8 double-buffers the accumulator (2 x 256 TMEM columns) so the epilogue of
 // one tile overlaps the main loop of the next. (FP8 problems with more than
 // 128 rows run on the CTA-pair kernel of gplk_gemm_pair.cu instead.) NVFP4
@@ -62,7 +64,9 @@ struct Traits {
 template <bool NVF4, int BN = 256>
 struct __align__(1024) Smem {
     uint8_t stage[Traits<NVF4, BN>::kStages][Traits<NVF4, BN>::kStageBytes];
-    uint8_t out_stage[NVF4 ? 128 * 32 * 2 : 16];  // NVFP4 epilogue staging: 128 rows x 32 BF16
+    // Epilogue staging, [column][row] BF16 chunks of 128 rows x 32 columns:
+    // one for NVFP4 (its ring leaves room for one), two for FP8.
+    uint8_t out_stage[NVF4 ? 1 : 2][128 * 32 * 2];
     uint64_t full[Traits<NVF4, BN>::kStages];
     uint64_t empty[Traits<NVF4, BN>::kStages];
     uint64_t acc_full[2];
@@ -84,7 +88,7 @@ struct Params {
     int m_tiles, n_tiles, k_stages;
     int sf_kblocks4;       // NVFP4: ceil(K / 64) = 512-byte blocks per 128 rows
     int sf_row_blocks_b;   // NVFP4: ceil(N / 128) row blocks in SFB
-    int tma_store;         // pair kernel: write D with TMA stores (M % 8 == 0)
+    int tma_store;         // write D with TMA stores (M % 8 == 0, 16-byte aligned D)
 };
 
 __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int& mt, int& nt,
@@ -274,6 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float scale = NVF4 ? __ldg(p.scale_a) : __ldg(p.scale_a) * __ldg(p.scale_b);
         int acc = 0;
         uint32_t acc_phase = 0;
+        uint32_t chunk_seq = 0;  // FP8 staging buffer rotation
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
             int mt, nt;
             tile_coords(t, p.m_tiles, p.n_tiles, mt, nt, p.group_m);
@@ -308,7 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // One 8 KiB staging buffer ([column][row] BF16, 32 columns):
                     // wait for the previous store to read it, fill, store.
                     const bool issuer = warp == 2 && lane == 0;
-                    uint16_t* stg = reinterpret_cast<uint16_t*>(sm.out_stage);
+                    uint16_t* stg = reinterpret_cast<uint16_t*>(sm.out_stage[0]);
                     const int m0 = mt * BM;
 #pragma unroll
                     for (int c = 0; c < 8; ++c) {
@@ -335,34 +340,68 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             } else {
+                // FP8: per 32-column chunk, tcgen05.ld, scale, BF16; the
+                // accumulator is released after its last chunk is in
+                // registers. With TMA stores (M % 8 == 0, aligned D) each
+                // chunk is staged [column][row] in one of two shared buffers
+                // and written by one TMA store, so the store of one chunk
+                // overlaps the staging of the next; otherwise each thread
+                // writes its row with plain stores.
+                const bool issuer = warp == 2 && lane == 0;
+                const int m0 = mt * BM;
 #pragma unroll 1
                 for (int c = 0; c < BN / 32; ++c) {
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(t_addr + 32u * c, r);
                     tmem_ld_wait();
-                    if (m < p.M) {
+                    if (c == BN / 32 - 1) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&sm.acc_empty[acc]);
+                    }
+                    uint32_t packed[16];
 #pragma unroll
-                        for (int j = 0; j < 32; j += 2) {
-                            const uint32_t v = pack_bf16x2(__uint_as_float(r[j]) * scale,
-                                                           __uint_as_float(r[j + 1]) * scale);
-                            const int n = n_base + 32 * c + j;
-                            if (n < p.N) drow[(size_t)n * ldd] = (uint16_t)(v & 0xFFFFu);
-                            if (n + 1 < p.N) drow[(size_t)(n + 1) * ldd] = (uint16_t)(v >> 16);
+                    for (int j = 0; j < 16; ++j)
+                        packed[j] = pack_bf16x2(__uint_as_float(r[2 * j]) * scale, __uint_as_float(r[2 * j + 1]) * scale);
+                    if (p.tma_store) {
+                        uint16_t* stg = reinterpret_cast<uint16_t*>(sm.out_stage[chunk_seq & 1u]);
+                        if (issuer) bulk_wait_read<1>();  // the store that last used this buffer has read it
+                        named_sync(1, 128);
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            stg[(2 * j) * 128 + row_in_tile] = (uint16_t)(packed[j] & 0xFFFFu);
+                            stg[(2 * j + 1) * 128 + row_in_tile] = (uint16_t)(packed[j] >> 16);
+                        }
+                        fence_proxy_async_smem();
+                        named_sync(1, 128);
+                        if (issuer && n_base + 32 * c < p.N) {
+                            tma_store_2d(&tmD, stg, m0, n_base + 32 * c);
+                            bulk_commit();
+                        }
+                        ++chunk_seq;
+                    } else if (m < p.M) {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const int n = n_base + 32 * c + 2 * j;
+                            if (n < p.N) drow[(size_t)n * ldd] = (uint16_t)(packed[j] & 0xFFFFu);
+                            if (n + 1 < p.N) drow[(size_t)(n + 1) * ldd] = (uint16_t)(packed[j] >> 16);
                         }
                     }
                 }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&sm.acc_empty[acc]);
             }
             if (++acc == TR::kAccBufs) {
                 acc = 0;
                 acc_phase ^= 1u;
             }
         }
-        if (NVF4 && p.tma_store && warp == 2 && lane == 0) bulk_wait<0>();
+        if (p.tma_store && warp == 2 && lane == 0) bulk_wait<0>();  // every store of D has completed
     }
 
+    // The role branches above leave warps 0 and 1 diverged (one lane works,
+    // the others skip ahead): reconverge each warp before the block-wide
+    // barrier, which must see all of a warp's threads together, so TMEM is
+    // freed only after every epilogue warp has finished reading it.
+    __syncwarp();
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
@@ -423,7 +462,7 @@ static int launch(const uint8_t* A, const uint8_t* B, const uint8_t* SFA, const 
     p.group_m = NVF4 ? 32 : kGroupM;
     CUtensorMap tmD;
     memset(&tmD, 0, sizeof(tmD));
-    p.tma_store = NVF4 && (M % 8 == 0) && aligned16(D);
+    p.tma_store = (M % 8 == 0) && aligned16(D);
     if (p.tma_store) {
         st = encode_tmap_2d_u16(&tmD, D, (uint64_t)M, (uint64_t)N, (uint64_t)M * 2, 128, 32);
         if (st != GPLK_STATUS_OK) return st;

@@ -298,6 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1) pv_kernel(const Params p) {
     if (keep == 1.2345678e-30f) p.sink[0] = keep;  // never true; keeps the work live
     if (p.verify_out) p.verify_out[(size_t)global_warp * 32 + lane] = keep_bits;
 
+    __syncwarp();  // roles leave lanes diverged: reconverge before the block-wide barrier
     tc_fence_before();
     __syncthreads();
     if (sm.has_tmem) {
@@ -314,6 +315,7 @@ __global__ void __launch_bounds__(kThreads, 1) pv_kernel(const Params p) {
                 for (int j = 0; j < 16; ++j) p.mma_out[(size_t)row * 256 + c * 16 + j] = __uint_as_float(r[j]);
             }
         }
+        __syncwarp();
         tc_fence_before();
         __syncthreads();
         if (role == GPLK_PV_ROLE_TENSOR && rank == 0) {
