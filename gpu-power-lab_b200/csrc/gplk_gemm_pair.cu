@@ -474,10 +474,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (issuer) bulk_wait<0>();  // every store of D has completed
     }
 
-    // The role branches above leave warps 0 and 1 diverged (one lane works,
-    // the others skip ahead): reconverge each warp before the cluster-wide
-    // barrier, so TMEM is freed only after every epilogue warp of both CTAs
-    // has finished reading it.
+    // Warps 0 and 1 arrive here diverged (one lane ran the producer or MMA
+    // loop): reconverge them, then the cluster-wide barrier holds the TMEM
+    // release until every epilogue warp of both CTAs has finished reading it.
     __syncwarp();
     tc_fence_before();
     cluster_sync();

@@ -397,10 +397,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (p.tma_store && warp == 2 && lane == 0) bulk_wait<0>();  // every store of D has completed
     }
 
-    // The role branches above leave warps 0 and 1 diverged (one lane works,
-    // the others skip ahead): reconverge each warp before the block-wide
-    // barrier, which must see all of a warp's threads together, so TMEM is
-    // freed only after every epilogue warp has finished reading it.
+    // Warps 0 and 1 arrive here diverged (one lane ran the producer or MMA
+    // loop): reconverge them, then the block-wide barrier holds the TMEM
+    // release until every epilogue warp has finished reading it.
     __syncwarp();
     tc_fence_before();
     __syncthreads();
