@@ -20,8 +20,10 @@
 //         FP32 (at least as accurate) and rounds once to FP16.
 // D is always M x N column-major.
 //
-// A persistent grid of 2-CTA clusters walks 256 x 256 output tiles in a
-// grouped order (raster groups along M; odd groups walk N backwards). It is
+// A persistent grid of 2-CTA clusters walks 256 x BN output tiles (BN = 256;
+// 128 for problems too small to fill the SMs with 256-wide tiles, see
+// tile_plan) in a grouped order (raster groups along M; odd groups walk N
+// backwards). It is
 // launched with programmatic stream serialisation, so its set-up overlaps
 // the previous GEMM on the stream. Per cluster, one tcgen05.mma.cta_group::2 (M = 256,
 // N = 256) per 32 bytes of K; each CTA TMA-loads its own 128 rows of the A
@@ -50,9 +52,21 @@ enum class Out { BF16, F16, F32, S32 };
 constexpr int kThreads = 192;
 constexpr int kSlab = 128 * 128;          // one CTA's 128 rows x 128 bytes of K
 constexpr int kSlabs = 2;                 // K slabs per stage (8 MMAs)
-constexpr int kStages = 3;
-constexpr int kOperandBytes = kSlabs * kSlab;    // A (or B) part of a stage: 32 KiB
-constexpr int kStageBytes = 2 * kOperandBytes;   // 64 KiB per CTA
+constexpr int kOperandBytes = kSlabs * kSlab;    // A part of a stage: 32 KiB
+
+// Pair-tile geometry for tile width BN (the pair computes 256 x BN; each CTA
+// holds 128 rows of A and BN / 2 rows of B per K slab). Narrower tiles have
+// smaller stages, so their rings are deeper in the same shared memory.
+template <int BN>
+struct Geom {
+    static_assert(BN == 256 || BN == 128, "pair tile width");
+    static constexpr int kBRows = BN / 2;
+    static constexpr int kBSlab = kBRows * 128;
+    static constexpr int kBOperand = kSlabs * kBSlab;
+    static constexpr int kStageBytes = kOperandBytes + kBOperand;  // 64 / 48 KiB per CTA
+    static constexpr int kStages = BN == 256 ? 3 : 4;
+    static constexpr uint32_t kTmemCols = 2u * (uint32_t)BN;  // double-buffered accumulator
+};
 constexpr int kMaxGroupM = 16;            // raster group along M (pair tiles), bounds
 constexpr int kMinGroupM = 8;
 #ifndef GPLK_PAIR_PANEL_BUDGET
@@ -92,12 +106,13 @@ struct Cfg {
     static constexpr uint32_t kADescLayout = kA32BAtoms ? 1u : 2u;
     static constexpr uint32_t kASbo = kA32BAtoms ? 512u : 1024u;
     static constexpr int kChunkCols = kOutChunkBytes / (128 * kOutBytes);  // 32 or 16
-    static constexpr int kChunks = 256 / kChunkCols;
-    // Instruction descriptor (M = 256, N = 256, B K-major).
-    static constexpr uint32_t kIdesc = ((KIND == Kind::I8 ? 2u : 1u) << 4)  // D: S32 or F32
-                                       | (FMT << 7) | (FMT << 10)              // A, B formats
-                                       | ((A_KMAJOR ? 0u : 1u) << 15)          // A major-ness
-                                       | ((256u >> 3) << 17) | ((256u >> 4) << 24);
+    // Instruction descriptor (M = 256, N = n, B K-major).
+    __host__ __device__ static constexpr uint32_t idesc(uint32_t n) {
+        return ((KIND == Kind::I8 ? 2u : 1u) << 4)  // D: S32 or F32
+               | (FMT << 7) | (FMT << 10)           // A, B formats
+               | ((A_KMAJOR ? 0u : 1u) << 15)       // A major-ness
+               | ((n >> 3) << 17) | ((256u >> 4) << 24);
+    }
 };
 
 using CfgFP8 = Cfg<Kind::F8F6F4, 0u, Out::BF16, true, true>;  // F8F6F4 format 0 = E4M3
@@ -175,11 +190,12 @@ struct Params {
     int accumulate; // beta = 1: D = A * B + D (D read before it is written)
 };
 
+template <int BN>
 struct __align__(1024) Smem {
-    uint8_t stage[kStages][kStageBytes];
+    uint8_t stage[Geom<BN>::kStages][Geom<BN>::kStageBytes];
     uint8_t out_stage[2][kOutChunkBytes];
-    uint64_t full[kStages];
-    uint64_t empty[kStages];
+    uint64_t full[Geom<BN>::kStages];
+    uint64_t empty[Geom<BN>::kStages];
     uint64_t acc_full[2];
     uint64_t acc_empty[2];
     uint64_t drain;
@@ -211,13 +227,16 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[N]) {
     }
 }
 
-template <class C>
+template <class C, int BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmD, const Params p) {
-    constexpr int S = kStages;
+    using G = Geom<BN>;
+    constexpr int S = G::kStages;
+    constexpr int kChunks = BN / C::kChunkCols;
     extern __shared__ uint8_t smem_raw[];
-    Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    Smem<BN>& sm =
+        *reinterpret_cast<Smem<BN>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const uint32_t warp = warp_id_uniform();
     const uint32_t lane = lane_id();
     const uint32_t rank = cluster_ctarank();
@@ -246,7 +265,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (p.tma_store) tma_prefetch_desc(&tmD);
     }
     if (warp == 1) {
-        tmem_alloc_pair(&sm.tmem_base, 512);
+        tmem_alloc_pair(&sm.tmem_base, G::kTmemCols);
         tmem_relinquish_pair();
     }
     tc_fence_before();
@@ -279,7 +298,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     }
                     uint8_t* st = sm.stage[stage];
                     const uint32_t full_leader = mapa_shared(smem_u32(&sm.full[stage]), 0);
-                    if (leader) mbar_arrive_expect_tx(&sm.full[stage], 2 * kStageBytes);
+                    if (leader) mbar_arrive_expect_tx(&sm.full[stage], 2 * G::kStageBytes);
 #pragma unroll
                     for (int sl = 0; sl < kSlabs; ++sl) {
                         const int kk = kb * kSlabs + sl;  // 128-byte slab of K
@@ -292,8 +311,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                 tma_load_2d_pair(a_dst + b * C::kABoxBytes, &tmA, full_leader,
                                                  (m_base + b * C::kRowElems) * C::kInBytes, kk * C::kRowElems);
                         }
-                        tma_load_2d_pair(st + kOperandBytes + sl * kSlab, &tmB, full_leader, kk * 128,
-                                         nt * 256 + (int)rank * 128);
+                        tma_load_2d_pair(st + kOperandBytes + sl * G::kBSlab, &tmB, full_leader, kk * 128,
+                                         nt * BN + (int)rank * G::kBRows);
                     }
                     issued_mask |= 1u << stage;
                     issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
@@ -324,7 +343,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d_tmem = tmem + (uint32_t)acc * 256u;
+                const uint32_t d_tmem = tmem + (uint32_t)acc * (uint32_t)BN;
                 for (int kb = 0; kb < p.k_stages; ++kb) {
                     if (!mbar_wait_cluster(&sm.full[stage], phase, &sm.abort, 0x0512)) {
                         ok = false;
@@ -336,12 +355,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int j = 0; j < 4 * kSlabs; ++j) {
                         const uint32_t slab = (uint32_t)(j >> 2) * kSlab, jj = (uint32_t)(j & 3);
+                        const uint32_t bslab = (uint32_t)(j >> 2) * (uint32_t)G::kBSlab;
                         const uint64_t a_desc =
                             C::kAKMajor ? desc_kmajor_sw128(a_addr + slab + 32u * jj)
                                         : desc_mnmajor(a_addr + slab + C::kAStep * jj, C::kABoxBytes, C::kASbo,
                                                        C::kADescLayout);
-                        mma_pair<C::kKind>(d_tmem, a_desc, desc_kmajor_sw128(b_addr + slab + 32u * jj), C::kIdesc,
-                                           (kb | j) != 0);
+                        mma_pair<C::kKind>(d_tmem, a_desc, desc_kmajor_sw128(b_addr + bslab + 32u * jj),
+                                           C::idesc((uint32_t)BN), (kb | j) != 0);
                     }
                     const uint32_t e = smem_u32(&sm.empty[stage]);
                     tc_commit_pair(mapa_shared(e, 0));
@@ -385,11 +405,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const int m0 = mt * 256 + (int)rank * 128;
             const int m = m0 + row_in_half;
-            const int n_base = nt * 256;
-            const uint32_t t_addr = tmem + ((quarter * 32u) << 16) + (uint32_t)acc * 256u;
+            const int n_base = nt * BN;
+            const uint32_t t_addr = tmem + ((quarter * 32u) << 16) + (uint32_t)acc * (uint32_t)BN;
             const uint32_t acc_empty_leader = mapa_shared(smem_u32(&sm.acc_empty[acc]), 0);
 #pragma unroll 1
-            for (int c = 0; c < C::kChunks; ++c) {
+            for (int c = 0; c < kChunks; ++c) {
                 uint32_t r[CC];
                 // beta = 1: this thread's row of the chunk's CC columns of the
                 // old D, loaded before the accumulator is read so the loads'
@@ -417,7 +437,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int j = 0; j < CC; ++j) r[j] = add_old<C::kOut>(r[j], old[j]);
                 }
-                if (c == C::kChunks - 1) {  // the accumulator is in registers: release it
+                if (c == kChunks - 1) {  // the accumulator is in registers: release it
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive_cluster(acc_empty_leader);
@@ -482,11 +502,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     cluster_sync();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc_pair(tmem, 512);
+        tmem_dealloc_pair(tmem, G::kTmemCols);
     }
 }
 
-constexpr int kSmemBytes = (int)sizeof(Smem) + 1024;
+template <int BN>
+constexpr int smem_bytes() {
+    return (int)sizeof(Smem<BN>) + 1024;
+}
 
 // 2-D tensor map over `rows` rows of `row_bytes` bytes (pitch `pitch`),
 // addressed in bytes, box 128 bytes x box_rows, 128-byte swizzle. Used for
@@ -497,9 +520,11 @@ static int encode_operand(CUtensorMap* map, const void* base, uint64_t row_bytes
     return encode_tmap_2d_u8(map, base, row_bytes, rows, row_bytes, 128, box_rows, swizzle);
 }
 
-template <class C>
-static int launch(const void* A, const void* B, void* D, int M, int N, int K, cudaStream_t stream,
-                  const float* scale_a = nullptr, const float* scale_b = nullptr, bool accumulate = false) {
+template <class C, int BN>
+static int launch_bn(const void* A, const void* B, void* D, int M, int N, int K, cudaStream_t stream,
+                     const float* scale_a, const float* scale_b, bool accumulate) {
+    using G = Geom<BN>;
+    constexpr int kSmemBytes = smem_bytes<BN>();
     DeviceInfo d;
     int st = require_sm100(&d);
     if (st != GPLK_STATUS_OK) return st;
@@ -509,8 +534,8 @@ static int launch(const void* A, const void* B, void* D, int M, int N, int K, cu
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return GPLK_STATUS_CUDA_ERROR;
     if (!(configured & (1ull << dev))) {
-        if (cudaFuncSetAttribute(gemm_pair_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
-            cudaSuccess)
+        if (cudaFuncSetAttribute(gemm_pair_kernel<C, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 kSmemBytes) != cudaSuccess)
             return GPLK_STATUS_LAUNCH_FAIL;
         configured |= 1ull << dev;
     }
@@ -527,7 +552,7 @@ static int launch(const void* A, const void* B, void* D, int M, int N, int K, cu
         cfg.attrs = &attr;
         cfg.numAttrs = 1;
         int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<C>, &cfg) != cudaSuccess || n <= 0) {
+        if (cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<C, BN>, &cfg) != cudaSuccess || n <= 0) {
             cudaGetLastError();
             n = d.sm_count / 2;
         }
@@ -543,8 +568,8 @@ static int launch(const void* A, const void* B, void* D, int M, int N, int K, cu
                             C::kA32BAtoms ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B);
     }
     if (st != GPLK_STATUS_OK) return st;
-    // B column-major K x N: N rows of K elements, boxes of 128 bytes (K) x 128 rows (N).
-    st = encode_operand(&tmB, B, (uint64_t)K * C::kInBytes, (uint64_t)N, 128);
+    // B column-major K x N: N rows of K elements, boxes of 128 bytes (K) x BN / 2 rows (N).
+    st = encode_operand(&tmB, B, (uint64_t)K * C::kInBytes, (uint64_t)N, (uint32_t)G::kBRows);
     if (st != GPLK_STATUS_OK) return st;
     Params p;
     memset(&p, 0, sizeof(p));
@@ -553,7 +578,7 @@ static int launch(const void* A, const void* B, void* D, int M, int N, int K, cu
     p.N = N;
     p.K = K;
     p.m_tiles = (M + 255) / 256;
-    p.n_tiles = (N + 255) / 256;
+    p.n_tiles = (N + BN - 1) / BN;
     p.scale_a = scale_a;
     p.scale_b = scale_b;
     p.accumulate = accumulate ? 1 : 0;
@@ -579,8 +604,59 @@ static int launch(const void* A, const void* B, void* D, int M, int N, int K, cu
     }
     const int tiles = p.m_tiles * p.n_tiles;
     const int clusters = capacity[dev] < tiles ? capacity[dev] : tiles;
-    return launch_status(launch_pdl(gemm_pair_kernel<C>, dim3(2 * clusters), dim3(kThreads), kSmemBytes, stream,
-                                    tmA, tmB, tmD, p));
+    return launch_status(launch_pdl(gemm_pair_kernel<C, BN>, dim3(2 * clusters), dim3(kThreads), kSmemBytes,
+                                    stream, tmA, tmB, tmD, p));
+}
+
+// Tile plan of one GEMM: the CTA-pair kernel with 256 x 256 or 256 x 128
+// tiles, or, where the caller has one (FP8, `single`), the single-CTA kernel
+// with 128 x 256 / 128 / 64 tiles. Problems that give the 256 x 256 pair
+// tiles at least one full wave keep them (fewest operand bytes per FLOP).
+// A smaller problem takes the candidate whose tiles, in a single wave, leave
+// the fewest SMs idle; at equal fill the single-CTA tile, then the wider one.
+// Measured with CUDA-graph replays on B200 (TFLOP/s, FP8 / BF16):
+//   1024^3  1-CTA 128x64 473 (pair 256x256 241) / pair 256x128 247 (256x256 195)
+//   1536^3  1-CTA 128x128 1116 (pair 256x128 844) / pair 256x128 630 (256x256 536)
+//   2048^3  1-CTA 128x256 1609 (pair 256x256 1421) / pair 256x256 995 (256x128 793)
+//   3072^3  pair 256x256 2195 (1-CTA 128x256 2153) / pair 256x256 1309
+// Pair tiles 256 x 64 were never the fastest (FP8 1024^3: 324) and are not built.
+struct TilePlan {
+    bool pair;
+    int bn;
+};
+
+static TilePlan tile_plan(int M, int N, int K, int sm_count, bool single) {
+    (void)K;
+    const long pair_slots = sm_count / 2;
+    const bool pair_ok = M > 128 || !single;
+    if (pair_ok && (long)((M + 255) / 256) * ((N + 255) / 256) >= pair_slots) return {true, 256};
+    struct Cand {
+        bool pair;
+        int bn;
+    };
+    // In order of preference at equal fill.
+    const Cand cands[5] = {{false, 256}, {true, 256}, {false, 128}, {true, 128}, {false, 64}};
+    TilePlan best{pair_ok, pair_ok ? 256 : 64};
+    double best_fill = -1.0;
+    for (const Cand& c : cands) {
+        if (c.pair ? !pair_ok : !single) continue;
+        const long tiles = (long)((M + (c.pair ? 255 : 127)) / (c.pair ? 256 : 128)) * ((N + c.bn - 1) / c.bn);
+        const long slots = c.pair ? pair_slots : sm_count;
+        if (tiles > slots) continue;  // more than one wave
+        const double fill = (double)tiles / (double)slots;
+        if (fill > best_fill + 1e-9) {
+            best_fill = fill;
+            best = {c.pair, c.bn};
+        }
+    }
+    return best;
+}
+
+template <class C>
+static int launch_pair(int bn, const void* A, const void* B, void* D, int M, int N, int K, cudaStream_t stream,
+                       const float* scale_a = nullptr, const float* scale_b = nullptr, bool accumulate = false) {
+    if (bn == 128) return launch_bn<C, 128>(A, B, D, M, N, K, stream, scale_a, scale_b, accumulate);
+    return launch_bn<C, 256>(A, B, D, M, N, K, stream, scale_a, scale_b, accumulate);
 }
 
 // Arguments shared by the four entry points. Operand pitches must be
@@ -593,7 +669,11 @@ static int checked_launch(const void* A, const void* B, void* D, int M, int N, i
     constexpr int align = 16 / C::kInBytes;
     if (K == 0 || M % align != 0 || K % align != 0) return GPLK_STATUS_BAD_ARG;
     if (!A || !B || !D || !aligned16(A) || !aligned16(B)) return GPLK_STATUS_BAD_ARG;
-    return launch<C>(A, B, D, M, N, K, stream, nullptr, nullptr, accumulate);
+    DeviceInfo d;
+    const int st = current_device_info(&d);
+    if (st != GPLK_STATUS_OK) return st;
+    const TilePlan plan = tile_plan(M, N, K, d.sm_count, false);
+    return launch_pair<C>(plan.bn, A, B, D, M, N, K, stream, nullptr, nullptr, accumulate);
 }
 
 }  // namespace pair

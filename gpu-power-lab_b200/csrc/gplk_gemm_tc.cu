@@ -2,13 +2,14 @@
 //   FP8   E4M3 x E4M3, per-tensor FP32 scales           (kind::f8f6f4)
 //   NVFP4 E2M1 x E2M1, UE4M3 scale per 16 K-elements     (kind::mxf4nvf4.block16)
 // both with FP32 accumulation in TMEM and BF16 output, in cuBLASLt's TN
-// convention (A and B K-major, D column-major M x N).
+// convention (A and B K-major, D column-major M x N). FP8 problems go to
+// this kernel or to the CTA-pair kernel of gplk_gemm_pair.cu by
+// pair::tile_plan.
 //
 // One persistent CTA per SM walks output tiles of 128 x BN in a grouped
 // (L2-friendly) order, launched with programmatic stream serialisation (its
-// set-up overlaps the previous GEMM on the stream). BN is 256 for NVFP4 and
-// for FP8 problems with a single 128-row block; small FP8 problems take
-// BN = 128 or 64 so their tiles cover more of the 148 SMs (1024^3 has 16
+// set-up overlaps the previous GEMM on the stream). BN is 256 for NVFP4;
+// FP8 takes BN = 256, 128 or 64 as pair::tile_plan decides (1024^3 has 16
 // CTA-pair tiles of 256 x 256 but 128 tiles of 128 x 64). Warp roles:
 //   warp 0      TMA producer: 2-D tiled loads of A (128 rows) and B (256
 //               rows), 128 bytes of K per stage with 128-byte swizzle, into a
@@ -21,9 +22,8 @@
 //               in shared memory and written by TMA stores (plain stores when
 //               D's rows are not 16-byte multiples). Warp w reads TMEM lanes
 //               32*(w%4)..+31 (= tile rows).
-// FP8 double-buffers the accumulator (2 x 256 TMEM columns) so the epilogue of
-// one tile overlaps the main loop of the next. (FP8 problems with more than
-// 128 rows run on the CTA-pair kernel of gplk_gemm_pair.cu instead.) NVFP4
+// FP8 double-buffers the accumulator (2 x BN TMEM columns) so the epilogue of
+// one tile overlaps the main loop of the next. NVFP4
 // needs TMEM for per-stage scale factors, so it keeps one accumulator and
 // drains it into registers before storing, releasing TMEM early.
 // Every mbarrier wait is bounded; on timeout the kernel records
@@ -472,33 +472,6 @@ static int launch(const uint8_t* A, const uint8_t* B, const uint8_t* SFA, const 
                                     tmA, tmB, tmD, p));
 }
 
-// FP8 tile shape: the CTA-pair kernel's 256 x 256 tiles, or single-CTA
-// 128 x BN tiles with BN = 256 / 128 / 64. Narrower tiles are considered
-// only when the widest choice fills less than nine tenths of one wave of
-// the SMs (small problems); each candidate is then scored by the slowest
-// SM's share of the output (waves x output elements per SM and tile), with
-// narrower tiles weighted for their lower operand reuse, and ties go to the
-// wider tile. Returns 0 for the pair kernel, else BN.
-static int fp8_tile(int M, int N, int sm_count) {
-    const bool pair = M > 128;
-    const long slots = pair ? sm_count / 2 : sm_count;
-    const long wide_tiles = pair ? (long)((M + 255) / 256) * ((N + 255) / 256) : (long)((N + 255) / 256);
-    int choice = pair ? 0 : 256;
-    if (10 * wide_tiles >= 9 * slots) return choice;
-    double best = (double)((wide_tiles + slots - 1) / slots) * (128.0 * 256.0);
-    const int widths[2] = {128, 64};
-    const double weight[2] = {1.1, 1.25};
-    for (int i = 0; i < 2; ++i) {
-        const long tiles = (long)((M + 127) / 128) * ((N + widths[i] - 1) / widths[i]);
-        const double cost = (double)((tiles + sm_count - 1) / sm_count) * (128.0 * widths[i]) * weight[i];
-        if (cost < best) {
-            best = cost;
-            choice = widths[i];
-        }
-    }
-    return choice;
-}
-
 }  // namespace gemm_tc
 }  // namespace gplk
 
@@ -510,14 +483,14 @@ extern "C" int gplk_gemm_fp8_tn(const uint8_t* A, const uint8_t* B, uint16_t* D,
     if (K == 0 || K % 16 != 0) return GPLK_STATUS_BAD_ARG;
     if (!A || !B || !D || !scale_a || !scale_b) return GPLK_STATUS_BAD_ARG;
     if (!aligned16(A) || !aligned16(B)) return GPLK_STATUS_BAD_ARG;
-    // Problems with at least two 128-row blocks run on CTA pairs (256 x 256
-    // tiles, cta_group::2, gplk_gemm_pair.cu); a single row block runs on
-    // single CTAs (128 x 256 tiles).
     DeviceInfo d;
     const int st = current_device_info(&d);
     if (st != GPLK_STATUS_OK) return st;
-    switch (gemm_tc::fp8_tile(M, N, d.sm_count)) {
-        case 0: return pair::launch<pair::CfgFP8>(A, B, D, M, N, K, stream, scale_a, scale_b);
+    // CTA-pair tiles (256 x 256 / 128) or single-CTA tiles (128 x 256 / 128 /
+    // 64), whichever fills the SMs best (pair::tile_plan).
+    const pair::TilePlan plan = pair::tile_plan(M, N, K, d.sm_count, true);
+    if (plan.pair) return pair::launch_pair<pair::CfgFP8>(plan.bn, A, B, D, M, N, K, stream, scale_a, scale_b);
+    switch (plan.bn) {
         case 128: return gemm_tc::launch<false, 128>(A, B, nullptr, nullptr, D, M, N, K, scale_a, scale_b, stream);
         case 64: return gemm_tc::launch<false, 64>(A, B, nullptr, nullptr, D, M, N, K, scale_a, scale_b, stream);
         default: return gemm_tc::launch<false, 256>(A, B, nullptr, nullptr, D, M, N, K, scale_a, scale_b, stream);
