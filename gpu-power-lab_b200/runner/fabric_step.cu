@@ -215,6 +215,23 @@ int gpl_fabric_step_init(const char **err) {
     g_stats.rank = rank;
     g_stats.world = world;
     g_stats.bytes = s.bytes;
+    // One untimed step, on every rank at the same point: the first launch of
+    // the allreduce (module load, NCCL's first collective) happens here, not
+    // inside the first cycle's timing.
+    {
+        cudaStream_t ws = nullptr;
+        const bool ok = cudaStreamCreateWithFlags(&ws, cudaStreamNonBlocking) == cudaSuccess &&
+                        gpl_fabric_step_enqueue(ws) == 0 && cudaStreamSynchronize(ws) == cudaSuccess;
+        if (ws) cudaStreamDestroy(ws);
+        s.pending = false;
+        int code = 0, site = 0;
+        if (!ok || gplk_status_read(&code, &site, 1) != GPLK_STATUS_OK || code != GPLK_STATUS_OK) {
+            cudaGetLastError();
+            *err = "fabric step: the warm-up allreduce failed";
+            gpl_fabric_step_free();
+            return -1;
+        }
+    }
     return 0;
 }
 

@@ -51,8 +51,9 @@ typedef struct {
 } gpl_fabric_stats_t;
 
 /* Reads the environment and sets the step up on the current device (the
- * rendezvous may wait for the other ranks). Returns 0 with no fabric
- * requested or when set up; -1 with *err set (static string) otherwise. */
+ * rendezvous may wait for the other ranks), then runs one untimed step on
+ * every rank. Returns 0 with no fabric requested or when set up; -1 with
+ * *err set (static string) otherwise. */
 int gpl_fabric_step_init(const char **err);
 
 /* True once gpl_fabric_step_init has set a step up. */
