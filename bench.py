@@ -518,6 +518,16 @@ def bench_gemm(args, dist: Dist) -> dict:
 
         dtype, workload = "f32", f"FP32 SGEMM C = A*B row-major, M=N=K={n}, U[-1,1)"
         launches_per_step = 2
+
+        def sgemm_library():
+            # cuBLAS in true FP32 (TF32 off), the library behind the reference
+            # rung's cublasGemmEx COMPUTE_32F call.
+            torch.backends.cuda.matmul.allow_tf32 = False
+            return torch.matmul(A, B)
+
+        case = {"flops": 2.0 * n ** 3, "ours": lambda: gplk.sgemm(A, B, C), "library": sgemm_library,
+                "library_name": "cuBLAS FP32 via torch.matmul (TF32 off)", "lib_view": lambda out: out,
+                "ours_view": lambda: C, "inputs": [A, B], "D": C}
     else:
         n = args.gemm_n or (16384 if w == "nvfp4" else 8192)
         case = _gemm_case(w, n, dev, stream, seed=31 + 7 * dist.rank)
@@ -582,7 +592,7 @@ def bench_gemm(args, dist: Dist) -> dict:
                      **({"scalar_ffma_measured": scalar_ffma} if scalar_ffma is not None else {})},
         "clocks": sampler.summary(),
         "gpu_launches": args.steps * (1 if w != "sgemm" else 1),
-        **(_sustained_extras(case, stream, dev, args.rung_seconds) if w != "sgemm" else {}),
+        **_sustained_extras(case, stream, dev, args.rung_seconds),
     }
 
 
