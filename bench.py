@@ -90,9 +90,9 @@ def parse_args():
                     help="memstream at N=1: skip the FP8 / NVFP4 GEMM and power rungs added to the line")
     ap.add_argument("--rung-seconds", type=float, default=1.5,
                     help="sustained run per GEMM rung arm (the power rung runs twice as long)")
-    ap.add_argument("--pv-cycle", action="store_true",
-                    help="memstream at N>1: also run a short in-phase powervirus duty cycle with the gplk fabric "
-                         "step and add its node power and fabric time to the line")
+    ap.add_argument("--no-pv-cycle", action="store_true",
+                    help="memstream at N>1: skip the short in-phase powervirus duty cycle (gplk fabric step per "
+                         "cycle) whose node power and fabric time are added to the line")
     ap.add_argument("--no-fabric-check", action="store_true",
                     help="memstream at N>1: skip the fabric step's parity check and timing added to the line")
     ap.add_argument("--elements", type=int, default=TRIAD_N,
@@ -1343,7 +1343,7 @@ def main():
             line["rungs"] = bench_rungs(args, dist)
         if args.workload == "memstream" and dist.world > 1 and not args.no_fabric_check:
             line["fabric"] = fabric_check(dist, args.fabric_mib, steps=10, warmup=3)
-        if args.workload == "memstream" and dist.world > 1 and args.pv_cycle:
+        if args.workload == "memstream" and dist.world > 1 and not args.no_pv_cycle:
             line["powervirus_cycle"] = pv_cycle(args, dist)
         if dist.rank == 0 and not args.no_cpu and args.workload == "memstream":
             line["cpu_baseline"] = cpu_triad_gbps(args.cpu_seconds)
