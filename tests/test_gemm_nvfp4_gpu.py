@@ -58,6 +58,20 @@ def test_nvfp4_ladder_sampled_vs_oracle(n, gplk, oracle, cuda):
     assert _rel_fro(got[pairs[:, 1], pairs[:, 0]], want) <= TOL
 
 
+@pytest.mark.parametrize("mnk", [(4096, 2048, 256), (2048, 4352, 512), (2560, 2304, 768)])
+def test_nvfp4_several_tiles_per_cta_short_k(mnk, gplk, oracle, cuda):
+    """More tiles than SMs, so each persistent CTA hands its accumulator from
+    tile to tile, with K of only 1 to 3 pipeline stages per tile."""
+    M, N, K = mnk
+    pa, sfa, pb, sfb, alpha = _operands(oracle, M, N, K, seed=M + N + K)
+    got = _run(gplk, pa, sfa, pb, sfb, alpha, K, cuda)
+    assert np.isfinite(got).all()
+    rng = np.random.default_rng(K)
+    pairs = np.stack([rng.integers(0, M, 4096), rng.integers(0, N, 4096)], axis=1)
+    want = oracle.gemm_nvfp4_tn(pa, pb, sfa, sfb, K, alpha, pairs)
+    assert _rel_fro(got[pairs[:, 1], pairs[:, 0]], want) <= TOL
+
+
 def test_nvfp4_rejects_bad_k(gplk, cuda):
     import torch
 
