@@ -340,8 +340,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             } else {
-                // FP8: per 32-column chunk, tcgen05.ld, scale, BF16; the
-                // accumulator is released after its last chunk is in
+                // FP8: per 32-column chunk, tcgen05.ld, scale, BF16. The load
+                // of chunk c + 1 is issued before chunk c is converted and
+                // stored, so the TMEM read latency hides behind that work;
+                // the accumulator is released once its last chunk is in
                 // registers. With TMA stores (M % 8 == 0, aligned D) each
                 // chunk is staged [column][row] in one of two shared buffers
                 // and written by one TMA store, so the store of one chunk
@@ -349,12 +351,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // writes its row with plain stores.
                 const bool issuer = warp == 2 && lane == 0;
                 const int m0 = mt * BM;
-#pragma unroll 1
-                for (int c = 0; c < BN / 32; ++c) {
-                    uint32_t r[32];
-                    tmem_ld_32x32b_x32(t_addr + 32u * c, r);
-                    tmem_ld_wait();
-                    if (c == BN / 32 - 1) {
+                constexpr int NC = BN / 32;
+                uint32_t rr[2][32];
+                tmem_ld_32x32b_x32(t_addr, rr[0]);
+                tmem_ld_wait();
+#pragma unroll
+                for (int c = 0; c < NC; ++c) {
+                    const int cur = c & 1;
+                    if (c + 1 < NC) {
+                        tmem_ld_32x32b_x32(t_addr + 32u * (c + 1), rr[cur ^ 1]);
+                    } else {
                         tc_fence_before();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&sm.acc_empty[acc]);
@@ -362,7 +368,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint32_t packed[16];
 #pragma unroll
                     for (int j = 0; j < 16; ++j)
-                        packed[j] = pack_bf16x2(__uint_as_float(r[2 * j]) * scale, __uint_as_float(r[2 * j + 1]) * scale);
+                        packed[j] = pack_bf16x2(__uint_as_float(rr[cur][2 * j]) * scale,
+                                                __uint_as_float(rr[cur][2 * j + 1]) * scale);
                     if (p.tma_store) {
                         uint16_t* stg = reinterpret_cast<uint16_t*>(sm.out_stage[chunk_seq & 1u]);
                         if (issuer) bulk_wait_read<1>();  // the store that last used this buffer has read it
@@ -387,6 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             if (n + 1 < p.N) drow[(size_t)(n + 1) * ldd] = (uint16_t)(packed[j] >> 16);
                         }
                     }
+                    if (c + 1 < NC) tmem_ld_wait();
                 }
             }
             if (++acc == TR::kAccBufs) {
