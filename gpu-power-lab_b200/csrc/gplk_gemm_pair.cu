@@ -234,6 +234,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     using G = Geom<BN>;
     constexpr int S = G::kStages;
     constexpr int kChunks = BN / C::kChunkCols;
+    static_assert(kChunks % 2 == 0, "the epilogue handles chunks in pairs");
     extern __shared__ uint8_t smem_raw[];
     Smem<BN>& sm =
         *reinterpret_cast<Smem<BN>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -408,13 +409,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const int n_base = nt * BN;
             const uint32_t t_addr = tmem + ((quarter * 32u) << 16) + (uint32_t)acc * (uint32_t)BN;
             const uint32_t acc_empty_leader = mapa_shared(smem_u32(&sm.acc_empty[acc]), 0);
-#pragma unroll 1
-            for (int c = 0; c < kChunks; ++c) {
-                uint32_t r[CC];
+            // One chunk of CC columns: chunk c's accumulator values are in
+            // `r` (loaded and waited for); the TMEM load of chunk c + 1 into
+            // `nx` is issued before chunk c is converted and stored, so its
+            // latency hides behind that work.
+            auto chunk = [&](int c, uint32_t (&r)[CC], uint32_t (&nx)[CC]) {
                 // beta = 1: this thread's row of the chunk's CC columns of the
-                // old D, loaded before the accumulator is read so the loads'
-                // latency overlaps the TMEM read (a warp reads 32 consecutive
-                // rows of one column: 64 or 128 contiguous bytes).
+                // old D (a warp reads 32 consecutive rows of one column: 64 or
+                // 128 contiguous bytes).
                 uint32_t old[CC];
                 if (p.accumulate) {
                     const bool row_ok = m < p.M;
@@ -431,16 +433,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         }
                     }
                 }
-                tmem_ld_cols<CC>(t_addr + (uint32_t)(CC * c), r);
-                tmem_ld_wait();
-                if (p.accumulate) {
-#pragma unroll
-                    for (int j = 0; j < CC; ++j) r[j] = add_old<C::kOut>(r[j], old[j]);
-                }
-                if (c == kChunks - 1) {  // the accumulator is in registers: release it
+                if (c + 1 < kChunks) {
+                    tmem_ld_cols<CC>(t_addr + (uint32_t)(CC * (c + 1)), nx);
+                } else {  // the whole accumulator is in registers: release it
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive_cluster(acc_empty_leader);
+                }
+                if (p.accumulate) {
+#pragma unroll
+                    for (int j = 0; j < CC; ++j) r[j] = add_old<C::kOut>(r[j], old[j]);
                 }
                 if (p.tma_store) {
                     uint8_t* stg = sm.out_stage[chunk_seq & 1u];
@@ -485,6 +487,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         }
                     }
                 }
+                if (c + 1 < kChunks) tmem_ld_wait();
+            };
+            uint32_t ra[CC], rb[CC];
+            tmem_ld_cols<CC>(t_addr, ra);
+            tmem_ld_wait();
+#pragma unroll 1
+            for (int c = 0; c < kChunks; c += 2) {  // kChunks is even
+                chunk(c, ra, rb);
+                chunk(c + 1, rb, ra);
             }
             if (++acc == 2) {
                 acc = 0;
