@@ -686,6 +686,16 @@ def _sustained(fn, stream, dev, seconds: float, skip_s: float = 0.3, graph: bool
             "power": sampler.power_stats(skip_s), "timing": how}
 
 
+def _energy_mj(sampler: "ClockSampler"):
+    """The device's NVML energy counter (mJ since the driver loaded), or None."""
+    if not sampler.ok:
+        return None
+    try:
+        return float(sampler.nv.nvmlDeviceGetTotalEnergyConsumption(sampler.h))
+    except Exception:
+        return None
+
+
 def _energy(tflops: float, run: dict) -> dict:
     clk, pw = run["clocks"], run["power"]
     out = {"sm_mhz": clk.get("sm_mhz"), "reasons": clk.get("reasons"), "avg_w": pw.get("avg_w")}
@@ -1018,18 +1028,52 @@ def fabric_check(dist: Dist, mib: int, steps: int, warmup: int) -> dict:
         torch.cuda.synchronize(dev)
         dist.barrier()
         res[name] = dist.max(e0.elapsed_time(e1)) / steps
+    # Watts: each implementation back to back for about 0.6 s (the same
+    # count on every rank, from the max-over-ranks times above), this rank's
+    # NVML power sampled and its energy counter read around the loop.
+    nbytes = count * 2
+    power = {}
+    for name, fn in (("gplk", lambda: fab.allreduce_bf16(count, stream=stream)),
+                     ("nccl", lambda: dist.pg.all_reduce(other))):
+        iters = max(20, int(600.0 / res[name]))
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        sampler = ClockSampler(dist.local, period_s=0.01)
+        mj0 = _energy_mj(sampler)
+        sampler.start()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(iters):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        sampler.stop()
+        mj1 = _energy_mj(sampler)
+        dist.barrier()
+        ms = dist.max(e0.elapsed_time(e1)) / iters
+        avg_w = sampler.power_stats(skip_s=0.15).get("avg_w") or 0.0
+        have = mj0 is not None and mj1 is not None
+        mj_tot = dist.sum((mj1 - mj0) / iters if have else 0.0)
+        all_have = dist.sum(1.0 if have else 0.0) == dist.world
+        power[name] = {"steps": iters, "ms": round(ms, 4),
+                       "busbw": round(rung.allreduce_busbw_gbs(nbytes, ms / 1e3, dist.world), 1),
+                       "avg_w_per_gpu": round(dist.sum(avg_w) / dist.world, 1),
+                       "mj_per_step_per_gpu": round(mj_tot / dist.world, 2) if all_have else None}
     code, site = gplk.status_read()
     dist.barrier()
     fab.close()
     status_ok = dist.sum(1.0 if code == 0 else 0.0) == dist.world
-    nbytes = count * 2
     bus = {k: rung.allreduce_busbw_gbs(nbytes, v / 1e3, dist.world) for k, v in res.items()}
     return {"impl": "gplk_fabric_allreduce_bf16 (NVLink peer loads/stores, no multicast)",
             "bytes": nbytes, "bitexact": bitexact, "status_ok": status_ok,
             "check": "every rank's seeded N(0,1) BF16 input gathered, summed in FP32 in rank order, rounded once",
             "ms_gplk": round(res["gplk"], 4), "busbw_gplk": round(bus["gplk"], 1),
             "ms_nccl": round(res["nccl"], 4), "busbw_nccl": round(bus["nccl"], 1),
-            "gplk_over_nccl": round(res["nccl"] / res["gplk"], 4), "steps": steps}
+            "gplk_over_nccl": round(res["nccl"] / res["gplk"], 4), "steps": steps,
+            "sustained": power,
+            "sustained_note": "about 0.6 s of back-to-back in-place allreduces per implementation; the buffer "
+                              "saturates to +-inf after a few dozen in-place sums, the same for both; per-GPU "
+                              "power and energy averaged over ranks"}
 
 
 # ------------------------------------------------------------ powervirus rung
