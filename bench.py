@@ -288,9 +288,10 @@ def host_threads() -> int:
         return os.cpu_count() or 1
 
 
-def cpu_triad_gbps(seconds: float, n: int = 1 << 28, threads: int = 0) -> dict:
+def cpu_triad_gbps(seconds: float, n: int = 1 << 28, threads: int = 0, single: bool = True) -> dict:
     """The host triad a = fmaf(s, c, b) (the oracle's restatement of the
-    triad) over n elements, repeated for about `seconds`, all cores."""
+    triad) over n elements, repeated for about `seconds`, all cores; with
+    `single`, also one thread for about a fifth of that."""
     sys.path.insert(0, str(REPO / "oracle"))
     import numpy as np
     import oracle
@@ -307,8 +308,19 @@ def cpu_triad_gbps(seconds: float, n: int = 1 << 28, threads: int = 0) -> dict:
         el = time.perf_counter() - t0
         if el >= seconds:
             break
-    return {"value": round(12 * n * reps / el / 1e9, 2), "unit": "GB/s", "cores": nthreads, "kind": "port",
-            "sample": f"{reps} host triads over 3 x 2^{n.bit_length() - 1} FP32 ({el:.1f} s)"}
+    out = {"value": round(12 * n * reps / el / 1e9, 2), "unit": "GB/s", "cores": nthreads, "kind": "port",
+           "sample": f"{reps} host triads over 3 x 2^{n.bit_length() - 1} FP32 ({el:.1f} s)"}
+    if single and nthreads > 1:
+        reps1, t1 = 0, time.perf_counter()
+        while True:
+            oracle.triad_into(a, b, c, TRIAD_S, 1)
+            reps1 += 1
+            el1 = time.perf_counter() - t1
+            if el1 >= seconds / 5:
+                break
+        out["single_thread_gbps"] = round(12 * n * reps1 / el1 / 1e9, 2)
+        out["single_thread_sample"] = f"{reps1} host triads on one thread ({el1:.1f} s)"
+    return out
 
 
 def cpu_sgemm_tflops(n: int, seconds: float) -> dict:
