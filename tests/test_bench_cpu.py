@@ -36,3 +36,13 @@ def test_reference_arm_other_ranks_print_nothing():
     res = subprocess.run([sys.executable, str(REPO / "bench.py"), "--impl", "reference", "--steps", "1",
                           "--warmup", "1"], capture_output=True, text=True, timeout=300, cwd=str(REPO), env=e)
     assert res.returncode == 0 and res.stdout.strip() == ""
+
+
+def test_host_triad_baseline_reports_one_thread_beside_all_cores():
+    sys.path.insert(0, str(REPO))
+    import bench
+
+    r = bench.cpu_triad_gbps(0.2, n=1 << 20, threads=2)
+    assert r["cores"] == 2 and r["value"] > 0 and r["kind"] == "port"
+    assert r["single_thread_gbps"] > 0 and "one thread" in r["single_thread_sample"]
+    assert "single_thread_gbps" not in bench.cpu_triad_gbps(0.1, n=1 << 20, threads=2, single=False)
