@@ -630,6 +630,8 @@ static int launch_bn(const void* A, const void* B, void* D, int M, int N, int K,
 //   1536^3  1-CTA 128x128 1116 (pair 256x128 844) / pair 256x128 630 (256x256 536)
 //   2048^3  1-CTA 128x256 1609 (pair 256x256 1421) / pair 256x256 995 (256x128 793)
 //   3072^3  pair 256x256 2195 (1-CTA 128x256 2153) / pair 256x256 1309
+// (With its TMEM loads pipelined, the single-CTA FP8 kernel then measured
+// 501 / 1203 / 1648 at 1024 / 1536 / 2048^3, widening its lead there.)
 // Pair tiles 256 x 64 were never the fastest (FP8 1024^3: 324) and are not built.
 struct TilePlan {
     bool pair;
