@@ -10,11 +10,14 @@
 // (L2-friendly) order, launched with programmatic stream serialisation (its
 // set-up overlaps the previous GEMM on the stream). BN is 256 for NVFP4;
 // FP8 takes BN = 256, 128 or 64 as pair::tile_plan decides (1024^3 has 16
-// CTA-pair tiles of 256 x 256 but 128 tiles of 128 x 64). Warp roles:
-//   warp 0      TMA producer: 2-D tiled loads of A (128 rows) and B (256
-//               rows), 128 bytes of K per stage with 128-byte swizzle, into a
-//               STAGES-deep shared-memory ring; NVFP4 adds 1-D bulk copies of
-//               the stage's scale-factor blocks. No cluster multicast.
+// CTA-pair tiles of 256 x 256 but 128 tiles of 128 x 64). NVFP4 runs a
+// last wave that would leave half the CTAs idle as 128 x 128 half tiles,
+// one per CTA (work items, item_tile). Warp roles:
+//   warp 0      TMA producer: 2-D tiled loads of A (128 rows) and B (BN
+//               rows; for NVFP4 in 128-row boxes, one per half), 128 bytes of
+//               K per stage with 128-byte swizzle, into a STAGES-deep
+//               shared-memory ring; NVFP4 adds 1-D bulk copies of the
+//               stage's scale-factor blocks. No cluster multicast.
 //   warp 1      owns TMEM; one thread issues the MMAs (4 per stage: K = 32
 //               FP8 or 64 FP4 elements per instruction) and, for NVFP4,
 //               the shared->TMEM copies of the scale factors first.
@@ -89,7 +92,21 @@ struct Params {
     int sf_kblocks4;       // NVFP4: ceil(K / 64) = 512-byte blocks per 128 rows
     int sf_row_blocks_b;   // NVFP4: ceil(N / 128) row blocks in SFB
     int tma_store;         // write D with TMA stores (M % 8 == 0, 16-byte aligned D)
+    // Work items: items below full_items are whole tiles (item = tile);
+    // the rest split the last wave's tiles into 128-column halves (NVFP4).
+    int full_items, num_items;
 };
+
+// Work item -> tile and column half (-1: the whole 128 x BN tile).
+__device__ __forceinline__ int item_tile(const Params& p, int item, int& half) {
+    if (item < p.full_items) {
+        half = -1;
+        return item;
+    }
+    const int u = item - p.full_items;
+    half = u & 1;
+    return p.full_items + (u >> 1);
+}
 
 __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int& mt, int& nt,
                                             int group_m = kGroupM) {
@@ -115,7 +132,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const uint32_t warp = warp_id_uniform();
     const uint32_t lane = lane_id();
-    const int num_tiles = p.m_tiles * p.n_tiles;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; ++i) {
@@ -157,7 +173,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t phase = 0;
             uint32_t issued_mask = 0, issued_parity = 0;  // for the abort drain
             bool ok = true;
-            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+            for (int it = blockIdx.x; it < p.num_items && ok; it += gridDim.x) {
+                int half;
+                const int t = item_tile(p, it, half);
                 int mt, nt;
                 tile_coords(t, p.m_tiles, p.n_tiles, mt, nt, p.group_m);
                 for (int kb = 0; kb < p.k_stages; ++kb) {
@@ -166,24 +184,45 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     uint8_t* st = sm.stage[stage];
-                    mbar_arrive_expect_tx(&sm.full[stage], TR::kStageBytes);
-                    tma_load_2d(st, &tmA, &sm.full[stage], kb * BK_BYTES, mt * BM);
-                    tma_load_2d(st + A_STAGE, &tmB, &sm.full[stage], kb * BK_BYTES, nt * BN);
                     if constexpr (NVF4) {
-                        // A stage covers K-blocks 4*kb .. 4*kb+3 of row block mt:
-                        // 2 KiB contiguous. B covers two row blocks 2*nt, 2*nt+1.
+                        // B arrives in 128-row boxes: both for a whole tile, the
+                        // item's own half (into the first half slot) otherwise.
+                        // The A stage covers K-blocks 4*kb .. 4*kb+3 of row block
+                        // mt (2 KiB contiguous); B's scales are row blocks 2*nt
+                        // and 2*nt + 1, or the half's own one.
                         const size_t blk = (size_t)p.sf_kblocks4;
                         const uint8_t* sa = p.sfa + ((size_t)mt * blk + (size_t)kb * 4) * 512;
-                        const uint8_t* sb0 = p.sfb + ((size_t)(2 * nt) * blk + (size_t)kb * 4) * 512;
-                        // A last tile with N % 256 <= 128 has no second row block;
-                        // its B rows are zero-filled by TMA and never stored, so
-                        // any in-bounds scale bytes will do.
-                        const int nb1 = (2 * nt + 1 < p.sf_row_blocks_b) ? 2 * nt + 1 : 2 * nt;
-                        const uint8_t* sb1 = p.sfb + ((size_t)nb1 * blk + (size_t)kb * 4) * 512;
                         uint8_t* dsf = st + A_STAGE + B_STAGE;
-                        bulk_load(dsf, sa, SFA_STAGE, &sm.full[stage]);
-                        bulk_load(dsf + SFA_STAGE, sb0, SFB_STAGE / 2, &sm.full[stage]);
-                        bulk_load(dsf + SFA_STAGE + SFB_STAGE / 2, sb1, SFB_STAGE / 2, &sm.full[stage]);
+                        if (half < 0) {
+                            mbar_arrive_expect_tx(&sm.full[stage], TR::kStageBytes);
+                            tma_load_2d(st, &tmA, &sm.full[stage], kb * BK_BYTES, mt * BM);
+                            tma_load_2d(st + A_STAGE, &tmB, &sm.full[stage], kb * BK_BYTES, nt * BN);
+                            tma_load_2d(st + A_STAGE + B_STAGE / 2, &tmB, &sm.full[stage], kb * BK_BYTES,
+                                        nt * BN + 128);
+                            const uint8_t* sb0 = p.sfb + ((size_t)(2 * nt) * blk + (size_t)kb * 4) * 512;
+                            // A last tile with N % 256 <= 128 has no second row
+                            // block; its B rows are zero-filled by TMA and never
+                            // stored, so any in-bounds scale bytes will do.
+                            const int nb1 = (2 * nt + 1 < p.sf_row_blocks_b) ? 2 * nt + 1 : 2 * nt;
+                            const uint8_t* sb1 = p.sfb + ((size_t)nb1 * blk + (size_t)kb * 4) * 512;
+                            bulk_load(dsf, sa, SFA_STAGE, &sm.full[stage]);
+                            bulk_load(dsf + SFA_STAGE, sb0, SFB_STAGE / 2, &sm.full[stage]);
+                            bulk_load(dsf + SFA_STAGE + SFB_STAGE / 2, sb1, SFB_STAGE / 2, &sm.full[stage]);
+                        } else {
+                            mbar_arrive_expect_tx(&sm.full[stage],
+                                                  A_STAGE + B_STAGE / 2 + SFA_STAGE + SFB_STAGE / 2);
+                            tma_load_2d(st, &tmA, &sm.full[stage], kb * BK_BYTES, mt * BM);
+                            tma_load_2d(st + A_STAGE, &tmB, &sm.full[stage], kb * BK_BYTES,
+                                        nt * BN + 128 * half);
+                            const uint8_t* sbh =
+                                p.sfb + ((size_t)(2 * nt + half) * blk + (size_t)kb * 4) * 512;
+                            bulk_load(dsf, sa, SFA_STAGE, &sm.full[stage]);
+                            bulk_load(dsf + SFA_STAGE, sbh, SFB_STAGE / 2, &sm.full[stage]);
+                        }
+                    } else {
+                        mbar_arrive_expect_tx(&sm.full[stage], TR::kStageBytes);
+                        tma_load_2d(st, &tmA, &sm.full[stage], kb * BK_BYTES, mt * BM);
+                        tma_load_2d(st + A_STAGE, &tmB, &sm.full[stage], kb * BK_BYTES, nt * BN);
                     }
                     issued_mask |= 1u << stage;
                     issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
@@ -205,13 +244,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            const uint32_t idesc = NVF4 ? idesc_nvf4(BM, BN) : idesc_e4m3_f32(BM, BN);
+            const uint32_t idesc_full = NVF4 ? idesc_nvf4(BM, BN) : idesc_e4m3_f32(BM, BN);
             int stage = 0;
             uint32_t phase = 0;
             int acc = 0;
             uint32_t acc_phase = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+            for (int it = blockIdx.x; it < p.num_items && ok; it += gridDim.x) {
+                int half;
+                (void)item_tile(p, it, half);
+                // A half item multiplies its 128 B rows (loaded into the first
+                // half slot) into accumulator columns 0..127, with N = 128.
+                const uint32_t idesc = (NVF4 && half >= 0) ? idesc_nvf4(BM, 128) : idesc_full;
+                const int sfb_halves = half < 0 ? 2 : 1;
                 if (!mbar_wait(&sm.acc_empty[acc], acc_phase ^ 1u, &sm.abort, 0x0211)) {
                     ok = false;
                     break;
@@ -236,9 +281,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                             tmem_cp_32x128b_warpx4(sf_col + 4 * j, smem_desc(sf_addr + 512 * j, 0, 128, 0));
 #pragma unroll
                             for (int h = 0; h < 2; ++h)
-                                tmem_cp_32x128b_warpx4(
-                                    sf_col + 16 + 8 * j + 4 * h,
-                                    smem_desc(sf_addr + SFA_STAGE + h * (SFB_STAGE / 2) + 512 * j, 0, 128, 0));
+                                if (h < sfb_halves)
+                                    tmem_cp_32x128b_warpx4(
+                                        sf_col + 16 + 8 * j + 4 * h,
+                                        smem_desc(sf_addr + SFA_STAGE + h * (SFB_STAGE / 2) + 512 * j, 0, 128, 0));
                         }
 #pragma unroll
                         for (int j = 0; j < 4; ++j) {
@@ -279,7 +325,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         int acc = 0;
         uint32_t acc_phase = 0;
         uint32_t chunk_seq = 0;  // FP8 staging buffer rotation
-        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+        for (int it = blockIdx.x; it < p.num_items; it += gridDim.x) {
+            int half;
+            const int t = item_tile(p, it, half);
             int mt, nt;
             tile_coords(t, p.m_tiles, p.n_tiles, mt, nt, p.group_m);
             // All four epilogue warps leave together if any of them gave up
@@ -289,22 +337,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (*(volatile int*)&sm.epi_fail) break;
             tc_fence_after();
             const int m = mt * BM + row_in_tile;
-            const int n_base = nt * BN;
+            const int n_base = nt * BN + (half > 0 ? 128 : 0);
             const uint32_t t_addr = tmem + ((quarter * 32u) << 16) + (uint32_t)acc * (uint32_t)BN;
             uint16_t* drow = p.D + m;  // column-major: D[m + n * M]
             const size_t ldd = (size_t)p.M;
             if constexpr (NVF4) {
-                // Drain all 256 columns to registers, release TMEM, then store.
+                // Drain the accumulator's columns (256, or 128 for a half
+                // item) to registers, release TMEM, then store.
+                const int nch = half < 0 ? 8 : 4;  // 32-column chunks
                 uint32_t packed[128];
 #pragma unroll
                 for (int c = 0; c < 8; ++c) {
-                    uint32_t r[32];
-                    tmem_ld_32x32b_x32(t_addr + 32u * c, r);
-                    tmem_ld_wait();
+                    if (c < nch) {
+                        uint32_t r[32];
+                        tmem_ld_32x32b_x32(t_addr + 32u * c, r);
+                        tmem_ld_wait();
 #pragma unroll
-                    for (int j = 0; j < 16; ++j)
-                        packed[c * 16 + j] = pack_bf16x2(__uint_as_float(r[2 * j]) * scale,
-                                                         __uint_as_float(r[2 * j + 1]) * scale);
+                        for (int j = 0; j < 16; ++j)
+                            packed[c * 16 + j] = pack_bf16x2(__uint_as_float(r[2 * j]) * scale,
+                                                             __uint_as_float(r[2 * j + 1]) * scale);
+                    }
                 }
                 tc_fence_before();
                 __syncwarp();
@@ -317,6 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int m0 = mt * BM;
 #pragma unroll
                     for (int c = 0; c < 8; ++c) {
+                        if (c >= nch) continue;  // uniform over the four warps
                         if (issuer) bulk_wait_read<0>();
                         named_sync(1, 128);
 #pragma unroll
@@ -334,6 +387,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 } else if (m < p.M) {
 #pragma unroll
                     for (int j = 0; j < 128; ++j) {
+                        if (j >= 16 * nch) continue;
                         const int n = n_base + 2 * j;
                         if (n < p.N) drow[(size_t)n * ldd] = (uint16_t)(packed[j] & 0xFFFFu);
                         if (n + 1 < p.N) drow[(size_t)(n + 1) * ldd] = (uint16_t)(packed[j] >> 16);
@@ -446,7 +500,8 @@ static int launch(const uint8_t* A, const uint8_t* B, const uint8_t* SFA, const 
     CUtensorMap tmA, tmB;
     st = encode_tmap_2d_u8(&tmA, A, row_bytes, (uint64_t)M, row_bytes, BK_BYTES, BM);
     if (st != GPLK_STATUS_OK) return st;
-    st = encode_tmap_2d_u8(&tmB, B, row_bytes, (uint64_t)N, row_bytes, BK_BYTES, BN);
+    // NVFP4 loads B in 128-row boxes (two per stage for a whole tile).
+    st = encode_tmap_2d_u8(&tmB, B, row_bytes, (uint64_t)N, row_bytes, BK_BYTES, NVF4 ? 128 : BN);
     if (st != GPLK_STATUS_OK) return st;
 
     Params p;
@@ -487,6 +542,18 @@ static int launch(const uint8_t* A, const uint8_t* B, const uint8_t* SFA, const 
     }
     const int tiles = p.m_tiles * p.n_tiles;
     const int grid = tiles < d.sm_count ? tiles : d.sm_count;
+    // NVFP4: when the last wave of tiles would leave at least half the CTAs
+    // idle, its tiles are split into 128-column halves, one per CTA, so the
+    // wave ends in about the time of a half tile (4096^3: 512 tiles = 3
+    // waves of 148 + 68, run as 3 waves + 136 halves). Every output element
+    // still sums its K-blocks in the same order.
+    const int rem = tiles % grid;
+    p.full_items = tiles;
+    p.num_items = tiles;
+    if (NVF4 && tiles > grid && rem > 0 && 2 * rem <= grid && N % BN == 0) {
+        p.full_items = tiles - rem;
+        p.num_items = p.full_items + 2 * rem;
+    }
     return launch_status(launch_pdl(gemm_tc_kernel<NVF4, BN>, dim3(grid), dim3(kThreads), (size_t)smem, stream,
                                     tmA, tmB, tmD, p));
 }

@@ -58,10 +58,13 @@ def test_nvfp4_ladder_sampled_vs_oracle(n, gplk, oracle, cuda):
     assert _rel_fro(got[pairs[:, 1], pairs[:, 0]], want) <= TOL
 
 
-@pytest.mark.parametrize("mnk", [(4096, 2048, 256), (2048, 4352, 512), (2560, 2304, 768)])
+@pytest.mark.parametrize("mnk", [(4096, 2048, 256), (2048, 4352, 512), (2560, 2304, 768), (2600, 2304, 512)])
 def test_nvfp4_several_tiles_per_cta_short_k(mnk, gplk, oracle, cuda):
     """More tiles than SMs, so each persistent CTA hands its accumulator from
-    tile to tile, with K of only 1 to 3 pipeline stages per tile."""
+    tile to tile, with K of only 1 to 3 pipeline stages per tile. The last
+    two shapes leave a last wave of at most half the CTAs (180 and 189 tiles
+    on 148 SMs), which runs as 128-column half tiles; the last has a ragged
+    final row of tiles (M = 2600)."""
     M, N, K = mnk
     pa, sfa, pb, sfb, alpha = _operands(oracle, M, N, K, seed=M + N + K)
     got = _run(gplk, pa, sfa, pb, sfb, alpha, K, cuda)
