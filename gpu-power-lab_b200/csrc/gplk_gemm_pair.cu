@@ -22,7 +22,8 @@
 //
 // A persistent grid of 2-CTA clusters walks 256 x BN output tiles (BN = 256;
 // 128 for problems too small to fill the SMs with 256-wide tiles, see
-// tile_plan) in a grouped order (raster groups along M; odd groups walk N
+// tile_plan; a short last wave of 256-wide tiles runs as 256 x 128 halves,
+// see item_tile) in a grouped order (raster groups along M; odd groups walk N
 // backwards). It is
 // launched with programmatic stream serialisation, so its set-up overlaps
 // the previous GEMM on the stream. Per cluster, one tcgen05.mma.cta_group::2 (M = 256,
@@ -65,6 +66,7 @@ struct Geom {
     static constexpr int kBOperand = kSlabs * kBSlab;
     static constexpr int kStageBytes = kOperandBytes + kBOperand;  // 64 / 48 KiB per CTA
     static constexpr int kStages = BN == 256 ? 3 : 4;
+    static constexpr int kBBox = 64;  // rows of B per TMA box (two per slab for BN = 256)
     static constexpr uint32_t kTmemCols = 2u * (uint32_t)BN;  // double-buffered accumulator
 };
 constexpr int kMaxGroupM = 16;            // raster group along M (pair tiles), bounds
@@ -188,7 +190,21 @@ struct Params {
     int group_m;    // raster group along M (pair tiles)
     int tma_store;  // stage the epilogue through shared memory and TMA-store it
     int accumulate; // beta = 1: D = A * B + D (D read before it is written)
+    // Work items: items below full_items are whole pair tiles (item = tile);
+    // the rest split the last wave's 256 x 256 tiles into 256 x 128 halves.
+    int full_items, num_items;
 };
+
+// Work item -> pair tile and column half (-1: the whole 256 x BN tile).
+__device__ __forceinline__ int item_tile(const Params& p, int item, int& half) {
+    if (item < p.full_items) {
+        half = -1;
+        return item;
+    }
+    const int u = item - p.full_items;
+    half = u & 1;
+    return p.full_items + (u >> 1);
+}
 
 template <int BN>
 struct __align__(1024) Smem {
@@ -244,7 +260,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const bool leader = rank == 0;
     const int cluster = (int)(blockIdx.x >> 1);
     const int nclusters = (int)(gridDim.x >> 1);
-    const int num_tiles = p.m_tiles * p.n_tiles;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; ++i) {
@@ -288,10 +303,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             uint32_t phase = 0;
             uint32_t issued_mask = 0, issued_parity = 0;
             bool ok = true;
-            for (int t = cluster; t < num_tiles && ok; t += nclusters) {
+            for (int it = cluster; it < p.num_items && ok; it += nclusters) {
+                int half;
+                const int t = item_tile(p, it, half);
                 int mt, nt;
                 tile_coords(t, p.m_tiles, p.n_tiles, p.group_m, mt, nt);
                 const int m_base = mt * 256 + (int)rank * 128;
+                // This CTA's B rows: kBRows of the tile, or, for a half item,
+                // its half's kBRows / 2 (the pair's N = 128 split over both
+                // CTAs), loaded into the first half of each slab's B region.
+                const int b_row = half < 0 ? nt * BN + (int)rank * G::kBRows
+                                           : nt * BN + 128 * half + (int)rank * (G::kBRows / 2);
+                const uint32_t stage_tx =
+                    half < 0 ? 2u * (uint32_t)G::kStageBytes : 2u * (uint32_t)(kOperandBytes + G::kBOperand / 2);
                 for (int kb = 0; kb < p.k_stages; ++kb) {
                     if (!mbar_wait_cluster(&sm.empty[stage], phase ^ 1u, &sm.abort, 0x0501)) {
                         ok = false;
@@ -299,7 +323,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     }
                     uint8_t* st = sm.stage[stage];
                     const uint32_t full_leader = mapa_shared(smem_u32(&sm.full[stage]), 0);
-                    if (leader) mbar_arrive_expect_tx(&sm.full[stage], 2 * G::kStageBytes);
+                    if (leader) mbar_arrive_expect_tx(&sm.full[stage], stage_tx);
 #pragma unroll
                     for (int sl = 0; sl < kSlabs; ++sl) {
                         const int kk = kb * kSlabs + sl;  // 128-byte slab of K
@@ -312,8 +336,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                 tma_load_2d_pair(a_dst + b * C::kABoxBytes, &tmA, full_leader,
                                                  (m_base + b * C::kRowElems) * C::kInBytes, kk * C::kRowElems);
                         }
-                        tma_load_2d_pair(st + kOperandBytes + sl * G::kBSlab, &tmB, full_leader, kk * 128,
-                                         nt * BN + (int)rank * G::kBRows);
+                        // B in boxes of kBBox rows (64 for 256-wide tiles).
+                        uint8_t* b_dst = st + kOperandBytes + sl * G::kBSlab;
+                        tma_load_2d_pair(b_dst, &tmB, full_leader, kk * 128, b_row);
+                        if (half < 0 && G::kBBox < G::kBRows)
+                            tma_load_2d_pair(b_dst + G::kBBox * 128, &tmB, full_leader, kk * 128, b_row + G::kBBox);
                     }
                     issued_mask |= 1u << stage;
                     issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
@@ -338,7 +365,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             int acc = 0;
             uint32_t acc_phase = 0;
             bool ok = true;
-            for (int t = cluster; t < num_tiles && ok; t += nclusters) {
+            for (int it = cluster; it < p.num_items && ok; it += nclusters) {
+                int half;
+                (void)item_tile(p, it, half);
+                const uint32_t idesc = C::idesc(half < 0 ? (uint32_t)BN : 128u);
                 if (!mbar_wait_cluster(&sm.acc_empty[acc], acc_phase ^ 1u, &sm.abort, 0x0511)) {
                     ok = false;
                     break;
@@ -362,7 +392,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                         : desc_mnmajor(a_addr + slab + C::kAStep * jj, C::kABoxBytes, C::kASbo,
                                                        C::kADescLayout);
                         mma_pair<C::kKind>(d_tmem, a_desc, desc_kmajor_sw128(b_addr + bslab + 32u * jj),
-                                           C::idesc((uint32_t)BN), (kb | j) != 0);
+                                           idesc, (kb | j) != 0);
                     }
                     const uint32_t e = smem_u32(&sm.empty[stage]);
                     tc_commit_pair(mapa_shared(e, 0));
@@ -397,16 +427,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         int acc = 0;
         uint32_t acc_phase = 0;
         uint32_t chunk_seq = 0;
-        for (int t = cluster; t < num_tiles; t += nclusters) {
+        for (int it = cluster; it < p.num_items; it += nclusters) {
+            int half;
+            const int t = item_tile(p, it, half);
             int mt, nt;
             tile_coords(t, p.m_tiles, p.n_tiles, p.group_m, mt, nt);
+            const int nch = half < 0 ? kChunks : kChunks / 2;  // chunks of this item (even)
             if (!mbar_wait_sleepy(&sm.acc_full[acc], acc_phase, &sm.abort, 0x0521, true)) sm.epi_fail = 1;
             named_sync(1, 128);
             if (*(volatile int*)&sm.epi_fail) break;
             tc_fence_after();
             const int m0 = mt * 256 + (int)rank * 128;
             const int m = m0 + row_in_half;
-            const int n_base = nt * BN;
+            const int n_base = nt * BN + (half > 0 ? 128 : 0);
             const uint32_t t_addr = tmem + ((quarter * 32u) << 16) + (uint32_t)acc * (uint32_t)BN;
             const uint32_t acc_empty_leader = mapa_shared(smem_u32(&sm.acc_empty[acc]), 0);
             // One chunk of CC columns: chunk c's accumulator values are in
@@ -433,7 +466,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         }
                     }
                 }
-                if (c + 1 < kChunks) {
+                if (c + 1 < nch) {
                     tmem_ld_cols<CC>(t_addr + (uint32_t)(CC * (c + 1)), nx);
                 } else {  // the whole accumulator is in registers: release it
                     tc_fence_before();
@@ -487,13 +520,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         }
                     }
                 }
-                if (c + 1 < kChunks) tmem_ld_wait();
+                if (c + 1 < nch) tmem_ld_wait();
             };
             uint32_t ra[CC], rb[CC];
             tmem_ld_cols<CC>(t_addr, ra);
             tmem_ld_wait();
 #pragma unroll 1
-            for (int c = 0; c < kChunks; c += 2) {  // kChunks is even
+            for (int c = 0; c < nch; c += 2) {  // nch is even
                 chunk(c, ra, rb);
                 chunk(c + 1, rb, ra);
             }
@@ -579,8 +612,9 @@ static int launch_bn(const void* A, const void* B, void* D, int M, int N, int K,
                             C::kA32BAtoms ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B);
     }
     if (st != GPLK_STATUS_OK) return st;
-    // B column-major K x N: N rows of K elements, boxes of 128 bytes (K) x BN / 2 rows (N).
-    st = encode_operand(&tmB, B, (uint64_t)K * C::kInBytes, (uint64_t)N, (uint32_t)G::kBRows);
+    // B column-major K x N: N rows of K elements, boxes of 128 bytes (K) x
+    // kBBox = 64 rows (N); a CTA's BN / 2 rows of a tile take BN / 128 boxes.
+    st = encode_operand(&tmB, B, (uint64_t)K * C::kInBytes, (uint64_t)N, (uint32_t)G::kBBox);
     if (st != GPLK_STATUS_OK) return st;
     Params p;
     memset(&p, 0, sizeof(p));
@@ -615,6 +649,18 @@ static int launch_bn(const void* A, const void* B, void* D, int M, int N, int K,
     }
     const int tiles = p.m_tiles * p.n_tiles;
     const int clusters = capacity[dev] < tiles ? capacity[dev] : tiles;
+    // A last wave of 256 x 256 tiles that would leave at least half the
+    // pairs idle runs as 256 x 128 halves, one per pair (4096^3: 256 tiles
+    // = 3 waves of 74 + 34, run as 3 waves + 68 halves). Each half loads
+    // only its columns of B and issues N = 128 MMAs; every output element
+    // still sums its K-blocks in the same order.
+    const int rem = tiles % clusters;
+    p.full_items = tiles;
+    p.num_items = tiles;
+    if (BN == 256 && tiles > clusters && rem > 0 && 2 * rem <= clusters && N % 256 == 0) {
+        p.full_items = tiles - rem;
+        p.num_items = p.full_items + 2 * rem;
+    }
     return launch_status(launch_pdl(gemm_pair_kernel<C, BN>, dim3(2 * clusters), dim3(kThreads), kSmemBytes,
                                     stream, tmA, tmB, tmD, p));
 }

@@ -45,7 +45,9 @@ def _run(gplk, qa, sa, qb, sb, cuda):
                                  (200, 300, 512), (129, 257, 144), (1, 1, 16), (640, 1280, 2048),
                                  (4352, 264, 128),   # 1-CTA 128 x 128 tiles (too few pair tiles for one wave)
                                  (4352, 2304, 128),  # pair tiles: 17 rows, a second, one-row raster group
-                                 (1536, 1536, 512), (1000, 1000, 1008)])  # 1-CTA 128 x 128 / 128 x 64 tiles
+                                 (1536, 1536, 512), (1000, 1000, 1008),  # 1-CTA 128 x 128 / 128 x 64 tiles
+                                 (2560, 2048, 256),  # 80 pair tiles: a short last wave run as 256 x 128 halves
+                                 (2600, 2048, 128)])  # the same with a ragged last row of tiles
 def test_fp8_full_vs_oracle(mnk, gplk, oracle, cuda):
     M, N, K = mnk
     qa, sa, qb, sb = _operands(oracle, M, N, K, seed=M * 7 + N)

@@ -59,9 +59,11 @@ def _rel(x: np.ndarray, ref: np.ndarray) -> float:
 
 # (4608, 384, 128) and (4352, 272, 64) give more than one raster group of
 # 256-row pair tiles (8 per group for 2- and 4-byte operands, 16 for INT8),
-# so odd groups walk N backwards, the last group ragged.
+# so odd groups walk N backwards, the last group ragged. (2560, 2048, 128)
+# has 80 pair tiles: more than one wave of pairs, the short last wave run as
+# 256 x 128 half tiles.
 SHAPES = [(256, 256, 256), (1024, 1024, 1024), (512, 384, 1024), (264, 520, 128), (128, 256, 512),
-          (768, 1, 64), (2048, 512, 4096), (4608, 384, 128), (4352, 272, 64)]
+          (768, 1, 64), (2048, 512, 4096), (4608, 384, 128), (4352, 272, 64), (2560, 2048, 128)]
 
 
 @pytest.mark.parametrize("prec", ["bf16", "f16", "tf32", "i8"])
@@ -158,7 +160,7 @@ def _old_d(prec: str, M: int, N: int, seed: int):
 
 @pytest.mark.parametrize("prec", ["bf16", "f16", "tf32", "i8"])
 @pytest.mark.parametrize("shape", [(256, 256, 256), (1024, 1024, 1024), (264, 520, 128), (768, 1, 64),
-                                   (4352, 272, 64)], ids=lambda s: "x".join(map(str, s)))
+                                   (4352, 272, 64), (2560, 2048, 64)], ids=lambda s: "x".join(map(str, s)))
 def test_accumulate_matches_oracle(prec, shape, gplk, oracle, cuda):
     """beta = 1 (the tensor stream's C = A * B + C): the old D is read and the
     product added before the single rounding; S32 wraps."""
