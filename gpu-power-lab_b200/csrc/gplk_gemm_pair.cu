@@ -336,7 +336,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                 tma_load_2d_pair(a_dst + b * C::kABoxBytes, &tmA, full_leader,
                                                  (m_base + b * C::kRowElems) * C::kInBytes, kk * C::kRowElems);
                         }
-                        // B in boxes of kBBox rows (64 for 256-wide tiles).
+                        // B in boxes of kBBox = 64 rows: one per slab for a
+                        // 128-wide tile or a half item, two for a 256-wide tile.
                         uint8_t* b_dst = st + kOperandBytes + sl * G::kBSlab;
                         tma_load_2d_pair(b_dst, &tmB, full_leader, kk * 128, b_row);
                         if (half < 0 && G::kBBox < G::kBRows)
