@@ -122,3 +122,26 @@ def test_fp8_rejects_bad_k(gplk, cuda):
     s = torch.ones(1, device=cuda)
     with pytest.raises(gplk.GplkError):
         gplk.gemm_fp8_tn(A, A, D, s, s)
+
+
+def test_fp8_split_last_wave_is_bit_identical(gplk, oracle, cuda):
+    """4096^3 on CTA pairs runs its short last wave as 256 x 128 half tiles;
+    the two 4096 x 2048 column halves, computed by separate calls whose last
+    wave is too full to split, must give the same bits."""
+    import torch
+
+    n = 4096
+    qa, sa, qb, sb = _operands(oracle, n, n, n, seed=4243)
+    A, B = torch.from_numpy(qa).to(cuda), torch.from_numpy(qb).to(cuda)
+    ta = torch.tensor([sa], dtype=torch.float32, device=cuda)
+    tb = torch.tensor([sb], dtype=torch.float32, device=cuda)
+    full = torch.empty((n, n), dtype=torch.bfloat16, device=cuda)
+    gplk.gemm_fp8_tn(A, B, full, ta, tb)
+    h = n // 2
+    parts = []
+    for i in range(2):
+        Dp = torch.empty((h, n), dtype=torch.bfloat16, device=cuda)
+        gplk.gemm_fp8_tn(A, B[i * h:(i + 1) * h].contiguous(), Dp, ta, tb)
+        parts.append(Dp)
+    torch.cuda.synchronize()
+    assert torch.equal(full.view(torch.int16), torch.cat(parts).view(torch.int16))

@@ -106,3 +106,29 @@ def test_nvfp4_vs_cublaslt(n, gplk, oracle, cuda):
     torch.cuda.synchronize()
     ref = ref.float().cpu().numpy().astype(np.float64)
     assert _rel_fro(ours, ref) <= TOL
+
+
+def test_nvfp4_split_last_wave_is_bit_identical(gplk, oracle, cuda):
+    """4096^3 runs its short last wave as 128-column half tiles; two calls
+    of 4096 x 2048 (256 tiles each: a last wave too full to split) give the
+    same columns without the split. The bits must agree: every output
+    element sums its K-blocks in the same order."""
+    import torch
+
+    n = 4096
+    pa, sfa, pb, sfb, alpha = _operands(oracle, n, n, n, seed=4242)
+    t = lambda x: torch.from_numpy(x).to(cuda)
+    A, SA, B, SB = t(pa), t(sfa), t(pb), t(sfb)
+    al = torch.tensor([alpha], dtype=torch.float32, device=cuda)
+    full = torch.empty((n, n), dtype=torch.bfloat16, device=cuda)
+    gplk.gemm_nvfp4_tn(A, B, SA, SB, full, n, al)
+    h = n // 2
+    sf_half = SB.numel() // 2  # row blocks 0..15, then 16..31
+    parts = []
+    for i in range(2):
+        Dp = torch.empty((h, n), dtype=torch.bfloat16, device=cuda)
+        gplk.gemm_nvfp4_tn(A, B[i * h:(i + 1) * h].contiguous(), SA,
+                           SB[i * sf_half:(i + 1) * sf_half].contiguous(), Dp, n, al)
+        parts.append(Dp)
+    torch.cuda.synchronize()
+    assert torch.equal(full.view(torch.int16), torch.cat(parts).view(torch.int16))
