@@ -113,7 +113,8 @@ static int encode_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t row_by
 // 2-D 16-bit tensor, row length `inner` elements, `outer` rows, row pitch
 // `pitch_bytes`; box inner x outer, no swizzle (for TMA stores of BF16 tiles).
 static int encode_tmap_2d_u16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
-                              uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_outer) {
+                              uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_outer,
+                              CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE) {
     auto enc = tensor_map_encoder();
     if (!enc) return GPLK_STATUS_UNSUPPORTED;
     cuuint64_t dims[2] = {inner, outer};
@@ -121,7 +122,7 @@ static int encode_tmap_2d_u16(CUtensorMap* map, const void* base, uint64_t inner
     cuuint32_t box[2] = {box_inner, box_outer};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? GPLK_STATUS_OK : GPLK_STATUS_BAD_ARG;
 }

@@ -67,8 +67,9 @@ struct Traits {
 template <bool NVF4, int BN = 256>
 struct __align__(1024) Smem {
     uint8_t stage[Traits<NVF4, BN>::kStages][Traits<NVF4, BN>::kStageBytes];
-    // Epilogue staging, [column][row] BF16 chunks of 128 rows x 32 columns:
-    // one for NVFP4 (its ring leaves room for one), two for FP8.
+    // Epilogue staging, 8 KiB BF16 chunks of 128 rows x 32 columns: one for
+    // NVFP4 ([column][row]; its ring leaves room for one), two for FP8 (each
+    // two 128-byte-swizzled TMA boxes of 64 rows x 32 columns).
     uint8_t out_stage[NVF4 ? 1 : 2][128 * 32 * 2];
     uint64_t full[Traits<NVF4, BN>::kStages];
     uint64_t empty[Traits<NVF4, BN>::kStages];
@@ -393,18 +394,76 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (n + 1 < p.N) drow[(size_t)(n + 1) * ldd] = (uint16_t)(packed[j] >> 16);
                     }
                 }
-            } else {
-                // FP8: per 32-column chunk, tcgen05.ld, scale, BF16. The load
-                // of chunk c + 1 is issued before chunk c is converted and
-                // stored, so the TMEM read latency hides behind that work;
-                // the accumulator is released once its last chunk is in
-                // registers. With TMA stores (M % 8 == 0, aligned D) each
-                // chunk is staged [column][row] in one of two shared buffers
-                // and written by one TMA store, so the store of one chunk
-                // overlaps the staging of the next; otherwise each thread
-                // writes its row with plain stores.
+            } else if (p.tma_store) {
+                // FP8 with TMA stores (M % 8 == 0, 16-byte aligned D). Per
+                // 32-column chunk each warp loads its 32 rows as two 16-lane
+                // tcgen05.ld.16x256b.x4, whose registers are mma fragments:
+                // thread t holds rows t/4 and t/4 + 8 at columns 2(t%4), +1 of
+                // every 8-column group. Scaled and rounded to BF16 pairs they
+                // go to shared memory through stmatrix .trans (each 8 x 8 block
+                // lands as 8 columns of 8 consecutive rows, 16 bytes each) in
+                // the 128-byte-swizzled layout of two 64-row x 32-column TMA
+                // store boxes, so a warp's 2 KiB take 16 conflict-free
+                // wavefronts (column-major 2-byte stores took 32 and 32
+                // instructions). The loads of chunk c + 1 are issued before
+                // chunk c is stored; the accumulator is released once its last
+                // chunk is in registers. Two staging buffers: the stores of
+                // one chunk overlap the staging of the next.
                 const bool issuer = warp == 2 && lane == 0;
                 const int m0 = mt * BM;
+                constexpr int NC = BN / 32;
+                const uint32_t lanes0 = tmem + ((quarter * 32u) << 16) + (uint32_t)acc * (uint32_t)BN;
+                const uint32_t lanes1 = lanes0 + (16u << 16);
+                // stmatrix: thread 8m + j gives the address of row j (a D
+                // column) of matrix m, which holds tile rows r0 .. r0 + 7.
+                const int r0 = (int)quarter * 32 + 8 * (int)(lane >> 3);
+                const uint32_t jr = lane & 7u;
+                const uint32_t box_off = (uint32_t)(r0 >> 6) * 4096u;  // rows 64..127: second box
+                const uint32_t chk = (uint32_t)((r0 & 63) >> 3);         // 16-byte unit within a 128-byte line
+                uint32_t x[2][2][16];
+                tmem_ld_16x256b_x4(lanes0, x[0][0]);
+                tmem_ld_16x256b_x4(lanes1, x[0][1]);
+                tmem_ld_wait();
+#pragma unroll
+                for (int c = 0; c < NC; ++c) {
+                    const int cur = c & 1;
+                    if (c + 1 < NC) {
+                        tmem_ld_16x256b_x4(lanes0 + 32u * (uint32_t)(c + 1), x[cur ^ 1][0]);
+                        tmem_ld_16x256b_x4(lanes1 + 32u * (uint32_t)(c + 1), x[cur ^ 1][1]);
+                    } else {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&sm.acc_empty[acc]);
+                    }
+                    uint8_t* stg = sm.out_stage[chunk_seq & 1u];
+                    if (issuer) bulk_wait_read<1>();  // the store that last used this buffer has read it
+                    named_sync(1, 128);
+                    const uint32_t sbase = smem_u32(stg) + box_off;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const uint32_t cc = (uint32_t)(8 * k) + jr;  // D column within the chunk
+                        const uint32_t addr = sbase + cc * 128u + ((chk ^ (cc & 7u)) << 4);
+                        auto pk = [&](int h, int i) {
+                            return pack_bf16x2(__uint_as_float(x[cur][h][i]) * scale,
+                                               __uint_as_float(x[cur][h][i + 1]) * scale);
+                        };
+                        stmatrix_x4_trans(addr, pk(0, 4 * k), pk(0, 4 * k + 2), pk(1, 4 * k), pk(1, 4 * k + 2));
+                    }
+                    fence_proxy_async_smem();
+                    named_sync(1, 128);
+                    if (issuer && n_base + 32 * c < p.N) {
+                        tma_store_2d(&tmD, stg, m0, n_base + 32 * c);
+                        if (m0 + 64 < p.M) tma_store_2d(&tmD, stg + 4096, m0 + 64, n_base + 32 * c);
+                        bulk_commit();
+                    }
+                    ++chunk_seq;
+                    if (c + 1 < NC) tmem_ld_wait();
+                }
+            } else {
+                // FP8 with plain stores (D's rows not 16-byte multiples): per
+                // 32-column chunk, tcgen05.ld of this thread's row, scale,
+                // BF16, stored column by column; the load of chunk c + 1 is
+                // issued before chunk c is stored.
                 constexpr int NC = BN / 32;
                 uint32_t rr[2][32];
                 tmem_ld_32x32b_x32(t_addr, rr[0]);
@@ -419,33 +478,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&sm.acc_empty[acc]);
                     }
-                    uint32_t packed[16];
-#pragma unroll
-                    for (int j = 0; j < 16; ++j)
-                        packed[j] = pack_bf16x2(__uint_as_float(rr[cur][2 * j]) * scale,
-                                                __uint_as_float(rr[cur][2 * j + 1]) * scale);
-                    if (p.tma_store) {
-                        uint16_t* stg = reinterpret_cast<uint16_t*>(sm.out_stage[chunk_seq & 1u]);
-                        if (issuer) bulk_wait_read<1>();  // the store that last used this buffer has read it
-                        named_sync(1, 128);
+                    if (m < p.M) {
 #pragma unroll
                         for (int j = 0; j < 16; ++j) {
-                            stg[(2 * j) * 128 + row_in_tile] = (uint16_t)(packed[j] & 0xFFFFu);
-                            stg[(2 * j + 1) * 128 + row_in_tile] = (uint16_t)(packed[j] >> 16);
-                        }
-                        fence_proxy_async_smem();
-                        named_sync(1, 128);
-                        if (issuer && n_base + 32 * c < p.N) {
-                            tma_store_2d(&tmD, stg, m0, n_base + 32 * c);
-                            bulk_commit();
-                        }
-                        ++chunk_seq;
-                    } else if (m < p.M) {
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) {
+                            const uint32_t pkd = pack_bf16x2(__uint_as_float(rr[cur][2 * j]) * scale,
+                                                             __uint_as_float(rr[cur][2 * j + 1]) * scale);
                             const int n = n_base + 32 * c + 2 * j;
-                            if (n < p.N) drow[(size_t)n * ldd] = (uint16_t)(packed[j] & 0xFFFFu);
-                            if (n + 1 < p.N) drow[(size_t)(n + 1) * ldd] = (uint16_t)(packed[j] >> 16);
+                            if (n < p.N) drow[(size_t)n * ldd] = (uint16_t)(pkd & 0xFFFFu);
+                            if (n + 1 < p.N) drow[(size_t)(n + 1) * ldd] = (uint16_t)(pkd >> 16);
                         }
                     }
                     if (c + 1 < NC) tmem_ld_wait();
@@ -537,7 +577,11 @@ static int launch(const uint8_t* A, const uint8_t* B, const uint8_t* SFA, const 
     memset(&tmD, 0, sizeof(tmD));
     p.tma_store = (M % 8 == 0) && aligned16(D);
     if (p.tma_store) {
-        st = encode_tmap_2d_u16(&tmD, D, (uint64_t)M, (uint64_t)N, (uint64_t)M * 2, 128, 32);
+        // NVFP4 stages [column][row] chunks of 128 rows; FP8 stages two
+        // 128-byte-swizzled boxes of 64 rows per chunk (see its epilogue).
+        st = NVF4 ? encode_tmap_2d_u16(&tmD, D, (uint64_t)M, (uint64_t)N, (uint64_t)M * 2, 128, 32)
+                  : encode_tmap_2d_u16(&tmD, D, (uint64_t)M, (uint64_t)N, (uint64_t)M * 2, 64, 32,
+                                       CU_TENSOR_MAP_SWIZZLE_128B);
         if (st != GPLK_STATUS_OK) return st;
     }
     const int tiles = p.m_tiles * p.n_tiles;
