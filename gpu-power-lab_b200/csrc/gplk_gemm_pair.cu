@@ -193,6 +193,7 @@ struct Params {
     // Work items: items below full_items are whole pair tiles (item = tile);
     // the rest split the last wave's 256 x 256 tiles into 256 x 128 halves.
     int full_items, num_items;
+    int frag_store;  // 2-byte D, TMA stores, beta = 0: staged by stmatrix into swizzled 64-row boxes
 };
 
 // Work item -> pair tile and column half (-1: the whole 256 x BN tile).
@@ -443,6 +444,63 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const int n_base = nt * BN + (half > 0 ? 128 : 0);
             const uint32_t t_addr = tmem + ((quarter * 32u) << 16) + (uint32_t)acc * (uint32_t)BN;
             const uint32_t acc_empty_leader = mapa_shared(smem_u32(&sm.acc_empty[acc]), 0);
+            bool staged = false;
+            if constexpr (C::kOutBytes == 2) {
+                if (p.frag_store) {
+                    // 2-byte D with TMA stores, beta = 0. Per 32-column chunk
+                    // each warp loads its 32 rows as two 16-lane
+                    // tcgen05.ld.16x256b.x4 (mma-fragment registers: thread t
+                    // holds rows t/4 and t/4 + 8 at columns 2(t%4), +1 of every
+                    // 8-column group), converts, and stages them with
+                    // stmatrix .trans in the 128-byte-swizzled layout of two
+                    // 64-row x 32-column TMA boxes: 16 conflict-free wavefronts
+                    // per warp and chunk instead of 32.
+                    const uint32_t lanes0 = t_addr;
+                    const uint32_t lanes1 = t_addr + (16u << 16);
+                    const int r0 = (int)quarter * 32 + 8 * (int)(lane >> 3);
+                    const uint32_t jr = lane & 7u;
+                    const uint32_t box_off = (uint32_t)(r0 >> 6) * 4096u;
+                    const uint32_t chk = (uint32_t)((r0 & 63) >> 3);
+                    auto fchunk = [&](int c, uint32_t (&x)[2][16]) {
+                        tmem_ld_16x256b_x4(lanes0 + 32u * (uint32_t)c, x[0]);
+                        tmem_ld_16x256b_x4(lanes1 + 32u * (uint32_t)c, x[1]);
+                        tmem_ld_wait();
+                        if (c + 1 == nch) {  // the whole accumulator is in registers: release it
+                            tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive_cluster(acc_empty_leader);
+                        }
+                        uint8_t* stg = sm.out_stage[chunk_seq & 1u];
+                        if (issuer) bulk_wait_read<1>();  // the store that last used this buffer has read it
+                        named_sync(1, 128);
+                        const uint32_t sbase = smem_u32(stg) + box_off;
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            const uint32_t cc = (uint32_t)(8 * k) + jr;  // D column within the chunk
+                            const uint32_t addr = sbase + cc * 128u + ((chk ^ (cc & 7u)) << 4);
+                            auto pk = [&](int h, int i) {
+                                const float lo = __uint_as_float(x[h][i]) * scale;
+                                const float hi = __uint_as_float(x[h][i + 1]) * scale;
+                                return C::kOut == Out::BF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
+                            };
+                            stmatrix_x4_trans(addr, pk(0, 4 * k), pk(0, 4 * k + 2), pk(1, 4 * k), pk(1, 4 * k + 2));
+                        }
+                        fence_proxy_async_smem();
+                        named_sync(1, 128);
+                        if (issuer && n_base + CC * c < p.N) {
+                            if (m0 < p.M) tma_store_2d(&tmD, stg, m0, n_base + CC * c);
+                            if (m0 + 64 < p.M) tma_store_2d(&tmD, stg + 4096, m0 + 64, n_base + CC * c);
+                            bulk_commit();
+                        }
+                        ++chunk_seq;
+                    };
+                    uint32_t xa[2][16];
+#pragma unroll 1
+                    for (int c = 0; c < nch; ++c) fchunk(c, xa);
+                    staged = true;
+                }
+            }
+            if (!staged) {
             // One chunk of CC columns: chunk c's accumulator values are in
             // `r` (loaded and waited for); the TMEM load of chunk c + 1 into
             // `nx` is issued before chunk c is converted and stored, so its
@@ -530,6 +588,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             for (int c = 0; c < nch; c += 2) {  // nch is even
                 chunk(c, ra, rb);
                 chunk(c + 1, rb, ra);
+            }
             }
             if (++acc == 2) {
                 acc = 0;
@@ -642,8 +701,15 @@ static int launch_bn(const void* A, const void* B, void* D, int M, int N, int K,
     p.k_stages = (K + C::kRowElems * kSlabs - 1) / (C::kRowElems * kSlabs);
     memset(&tmD, 0, sizeof(tmD));
     p.tma_store = ((size_t)M * C::kOutBytes) % 16 == 0 && aligned16(D);
+    p.frag_store = (C::kOutBytes == 2 && p.tma_store && !accumulate) ? 1 : 0;
     if (p.tma_store) {
-        st = C::kOutBytes == 2
+        // 2-byte D at beta = 0: two 128-byte-swizzled boxes of 64 rows per
+        // 32-column chunk (stmatrix staging); otherwise [column][row] chunks
+        // of 128 rows.
+        st = p.frag_store
+                 ? encode_tmap_2d_u16(&tmD, D, (uint64_t)M, (uint64_t)N, (uint64_t)M * 2, 64, C::kChunkCols,
+                                      CU_TENSOR_MAP_SWIZZLE_128B)
+             : C::kOutBytes == 2
                  ? encode_tmap_2d_u16(&tmD, D, (uint64_t)M, (uint64_t)N, (uint64_t)M * 2, 128, C::kChunkCols)
                  : encode_tmap_2d_u32(&tmD, D, (uint64_t)M, (uint64_t)N, (uint64_t)M * 4, 128, C::kChunkCols);
         if (st != GPLK_STATUS_OK) return st;
