@@ -344,12 +344,32 @@ __global__ void __launch_bounds__(kThreads, 1)
             const size_t ldd = (size_t)p.M;
             if constexpr (NVF4) {
                 // Drain the accumulator's columns (256, or 128 for a half
-                // item) to registers, release TMEM, then store.
+                // item) to registers, release TMEM, then store. With TMA
+                // stores the drain reads 16-lane mma fragments
+                // (tcgen05.ld.16x256b, as the FP8 epilogue below) for stmatrix
+                // staging; packed[16c + 4k + i] then holds 8 x 8 block i of
+                // column group k of chunk c. Plain stores keep this thread's
+                // row: packed[16c + j] = columns 32c + 2j, +1.
                 const int nch = half < 0 ? 8 : 4;  // 32-column chunks
                 uint32_t packed[128];
 #pragma unroll
                 for (int c = 0; c < 8; ++c) {
-                    if (c < nch) {
+                    if (c >= nch) continue;
+                    if (p.tma_store) {
+                        uint32_t x[2][16];
+                        const uint32_t lanes0 = tmem + ((quarter * 32u) << 16) + 32u * (uint32_t)c;
+                        tmem_ld_16x256b_x4(lanes0, x[0]);
+                        tmem_ld_16x256b_x4(lanes0 + (16u << 16), x[1]);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int k = 0; k < 4; ++k)
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                const int h = i >> 1, e = 4 * k + 2 * (i & 1);
+                                packed[c * 16 + 4 * k + i] = pack_bf16x2(__uint_as_float(x[h][e]) * scale,
+                                                                         __uint_as_float(x[h][e + 1]) * scale);
+                            }
+                    } else {
                         uint32_t r[32];
                         tmem_ld_32x32b_x32(t_addr + 32u * c, r);
                         tmem_ld_wait();
@@ -363,25 +383,33 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&sm.acc_empty[acc]);
                 if (p.tma_store) {
-                    // One 8 KiB staging buffer ([column][row] BF16, 32 columns):
-                    // wait for the previous store to read it, fill, store.
+                    // One 8 KiB staging buffer (two 128-byte-swizzled boxes of
+                    // 64 rows x 32 columns): wait for the previous store to
+                    // read it, fill it with stmatrix, store.
                     const bool issuer = warp == 2 && lane == 0;
-                    uint16_t* stg = reinterpret_cast<uint16_t*>(sm.out_stage[0]);
                     const int m0 = mt * BM;
+                    const int r0 = (int)quarter * 32 + 8 * (int)(lane >> 3);
+                    const uint32_t jr = lane & 7u;
+                    const uint32_t sbase = smem_u32(sm.out_stage[0]) + (uint32_t)(r0 >> 6) * 4096u;
+                    const uint32_t chk = (uint32_t)((r0 & 63) >> 3);
 #pragma unroll
                     for (int c = 0; c < 8; ++c) {
                         if (c >= nch) continue;  // uniform over the four warps
                         if (issuer) bulk_wait_read<0>();
                         named_sync(1, 128);
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            stg[(2 * j) * 128 + row_in_tile] = (uint16_t)(packed[c * 16 + j] & 0xFFFFu);
-                            stg[(2 * j + 1) * 128 + row_in_tile] = (uint16_t)(packed[c * 16 + j] >> 16);
+                        for (int k = 0; k < 4; ++k) {
+                            const uint32_t cc = (uint32_t)(8 * k) + jr;
+                            stmatrix_x4_trans(sbase + cc * 128u + ((chk ^ (cc & 7u)) << 4), packed[c * 16 + 4 * k],
+                                              packed[c * 16 + 4 * k + 1], packed[c * 16 + 4 * k + 2],
+                                              packed[c * 16 + 4 * k + 3]);
                         }
                         fence_proxy_async_smem();
                         named_sync(1, 128);
                         if (issuer && n_base + 32 * c < p.N) {
+                            const uint8_t* stg = sm.out_stage[0];
                             tma_store_2d(&tmD, stg, m0, n_base + 32 * c);
+                            if (m0 + 64 < p.M) tma_store_2d(&tmD, stg + 4096, m0 + 64, n_base + 32 * c);
                             bulk_commit();
                         }
                     }
@@ -577,11 +605,10 @@ static int launch(const uint8_t* A, const uint8_t* B, const uint8_t* SFA, const 
     memset(&tmD, 0, sizeof(tmD));
     p.tma_store = (M % 8 == 0) && aligned16(D);
     if (p.tma_store) {
-        // NVFP4 stages [column][row] chunks of 128 rows; FP8 stages two
-        // 128-byte-swizzled boxes of 64 rows per chunk (see its epilogue).
-        st = NVF4 ? encode_tmap_2d_u16(&tmD, D, (uint64_t)M, (uint64_t)N, (uint64_t)M * 2, 128, 32)
-                  : encode_tmap_2d_u16(&tmD, D, (uint64_t)M, (uint64_t)N, (uint64_t)M * 2, 64, 32,
-                                       CU_TENSOR_MAP_SWIZZLE_128B);
+        // Both stage each 32-column chunk as two 128-byte-swizzled boxes of
+        // 64 rows (stmatrix staging, see the epilogues).
+        st = encode_tmap_2d_u16(&tmD, D, (uint64_t)M, (uint64_t)N, (uint64_t)M * 2, 64, 32,
+                                CU_TENSOR_MAP_SWIZZLE_128B);
         if (st != GPLK_STATUS_OK) return st;
     }
     const int tiles = p.m_tiles * p.n_tiles;
